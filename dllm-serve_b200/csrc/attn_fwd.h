@@ -1,0 +1,33 @@
+// Internal launch interface of the sm_100a attention kernel (not part of the
+// public C ABI; see include/dllm_attn.h for that).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace dllm {
+
+struct AttnKernelArgs {
+  __nv_bfloat16* o;        // output rows, indexed like q
+  int64_t o_tok_stride;    // elements between consecutive output rows
+  int64_t o_head_stride;   // elements between heads inside a row
+  const int32_t* cu_q;     // [B+1] query rows (and output rows) per sequence
+  const int32_t* cu_k;     // [B+1] fresh key/value rows per sequence
+  const int32_t* cu_c;     // [B+1] cached key/value rows per sequence, or null
+  int B;
+  int Hq;
+  int Hkv;
+  int group;               // Hq / Hkv
+  float scale_log2;        // softmax_scale * log2(e)
+  int32_t* err;            // optional device status word
+};
+
+uint32_t attn_fwd_smem_bytes();
+
+cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                            const CUtensorMap& tmKc, const CUtensorMap& tmVc,
+                            const AttnKernelArgs& args, int max_q, cudaStream_t stream);
+
+}  // namespace dllm

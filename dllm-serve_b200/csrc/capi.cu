@@ -1,0 +1,291 @@
+// extern "C" entry points of libdllm_attn.so (declared in include/dllm_attn.h):
+// argument validation, TMA tensor-map encoding and kernel dispatch.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "dllm_attn.h"
+#include "attn_fwd.h"
+#include "kvcache.h"
+#include "select_kv.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DLLM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int num_sms_of_current_device() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 3-D map over [rows, heads, 128] bf16: dims (d, head, row), box (64, 1, 128),
+// 128-byte swizzle (matches the UMMA SW128 K-major / MN-major smem layout).
+int encode_rows_map(CUtensorMap* m, const void* ptr, int64_t rows, int heads, int64_t tok_stride) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return fail(DLLM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)(rows > 0 ? rows : 1)};
+  cuuint64_t strides[2] = {128 * 2, (cuuint64_t)tok_stride * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DLLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DLLM_OK;
+}
+
+int check_rows(const char* name, const void* p, int64_t tok_stride, int heads, int64_t rows) {
+  if (rows > 0 && p == nullptr) return fail(DLLM_ERR_INVALID_ARG, "%s is null", name);
+  if (!aligned(p, 16)) return fail(DLLM_ERR_ALIGNMENT, "%s is not 16-byte aligned", name);
+  if (tok_stride < (int64_t)heads * 128)
+    return fail(DLLM_ERR_INVALID_ARG, "%s token stride %lld < heads*head_dim", name,
+                (long long)tok_stride);
+  if (tok_stride % 8 != 0)
+    return fail(DLLM_ERR_ALIGNMENT, "%s token stride %lld is not a multiple of 8 elements", name,
+                (long long)tok_stride);
+  if (rows < 0) return fail(DLLM_ERR_INVALID_ARG, "%s has negative rows", name);
+  if (rows >= (int64_t)1 << 31) return fail(DLLM_ERR_TOO_LARGE, "%s has too many rows", name);
+  return DLLM_OK;
+}
+
+int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                const void* v, int64_t v_tok_stride, const void* kc, int64_t kc_tok_stride,
+                const void* vc, int64_t vc_tok_stride, void* o, int64_t o_tok_stride,
+                const int32_t* cu_q, const int32_t* cu_k, const int32_t* cu_c, int batch,
+                int max_q, int64_t total_q, int64_t total_k, int64_t total_c, int Hq, int Hkv,
+                int head_dim, float scale, int32_t* err, void* stream) {
+  if (head_dim != 128)
+    return fail(DLLM_ERR_UNSUPPORTED, "head_dim %d not supported (only 128)", head_dim);
+  if (Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
+    return fail(DLLM_ERR_UNSUPPORTED, "num_heads %d must be a positive multiple of num_kv_heads %d",
+                Hq, Hkv);
+  if (batch < 0 || max_q < 0 || total_q < 0 || total_k < 0 || total_c < 0)
+    return fail(DLLM_ERR_INVALID_ARG, "negative size");
+  if (!(scale > 0.f)) return fail(DLLM_ERR_INVALID_ARG, "softmax_scale must be > 0");
+  if (batch == 0 || total_q == 0 || max_q == 0) return DLLM_OK;
+  if (cu_q == nullptr || cu_k == nullptr) return fail(DLLM_ERR_INVALID_ARG, "cu_seqlens is null");
+  int rc;
+  if ((rc = check_rows("q", q, q_tok_stride, Hq, total_q)) != DLLM_OK) return rc;
+  if ((rc = check_rows("o", o, o_tok_stride, Hq, total_q)) != DLLM_OK) return rc;
+  if ((rc = check_rows("k", k, k_tok_stride, Hkv, total_k)) != DLLM_OK) return rc;
+  if ((rc = check_rows("v", v, v_tok_stride, Hkv, total_k)) != DLLM_OK) return rc;
+  if (cu_c != nullptr) {
+    if ((rc = check_rows("k_cached", kc, kc_tok_stride, Hkv, total_c)) != DLLM_OK) return rc;
+    if ((rc = check_rows("v_cached", vc, vc_tok_stride, Hkv, total_c)) != DLLM_OK) return rc;
+  }
+  CUtensorMap tq, tk, tv, tkc, tvc;
+  if ((rc = encode_rows_map(&tq, q, total_q, Hq, q_tok_stride)) != DLLM_OK) return rc;
+  if ((rc = encode_rows_map(&tk, k, total_k, Hkv, k_tok_stride)) != DLLM_OK) return rc;
+  if ((rc = encode_rows_map(&tv, v, total_k, Hkv, v_tok_stride)) != DLLM_OK) return rc;
+  if (cu_c != nullptr && total_c > 0) {
+    if ((rc = encode_rows_map(&tkc, kc, total_c, Hkv, kc_tok_stride)) != DLLM_OK) return rc;
+    if ((rc = encode_rows_map(&tvc, vc, total_c, Hkv, vc_tok_stride)) != DLLM_OK) return rc;
+  } else {
+    tkc = tk;
+    tvc = tv;
+    if (total_c == 0) cu_c = nullptr;
+  }
+  dllm::AttnKernelArgs a;
+  a.o = reinterpret_cast<__nv_bfloat16*>(o);
+  a.o_tok_stride = o_tok_stride;
+  a.o_head_stride = 128;
+  a.cu_q = cu_q;
+  a.cu_k = cu_k;
+  a.cu_c = cu_c;
+  a.B = batch;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.group = Hq / Hkv;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.err = err;
+  cudaError_t e = dllm::launch_attn_fwd(tq, tk, tv, tkc, tvc, a, max_q,
+                                        reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
+  return DLLM_OK;
+}
+
+int kv_copy_common(bool store, const void* key, int64_t key_stride, const void* value,
+                   int64_t value_stride, const void* k_cache, const void* v_cache,
+                   const int32_t* slots, int64_t n_tokens, int64_t row_elems, int elem_bytes,
+                   int64_t num_slots, int32_t* err, void* stream) {
+  if (n_tokens < 0 || row_elems <= 0 || num_slots < 0)
+    return fail(DLLM_ERR_INVALID_ARG, "negative size");
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8)
+    return fail(DLLM_ERR_INVALID_ARG, "elem_bytes %d not in {1,2,4,8}", elem_bytes);
+  if (n_tokens == 0) return DLLM_OK;
+  if (!key || !value || !k_cache || !v_cache || !slots)
+    return fail(DLLM_ERR_INVALID_ARG, "null pointer");
+  if (key_stride < row_elems || value_stride < row_elems)
+    return fail(DLLM_ERR_INVALID_ARG, "token stride smaller than the cache row");
+  dllm::KvCopyArgs a;
+  a.key = const_cast<void*>(key);
+  a.value = const_cast<void*>(value);
+  a.key_stride_bytes = key_stride * elem_bytes;
+  a.value_stride_bytes = value_stride * elem_bytes;
+  a.k_cache = const_cast<void*>(k_cache);
+  a.v_cache = const_cast<void*>(v_cache);
+  a.slots = slots;
+  a.n_tokens = n_tokens;
+  a.row_bytes = row_elems * elem_bytes;
+  a.num_slots = num_slots;
+  a.err = err;
+  int vec = 16;
+  auto fits = [&](int w) {
+    return aligned(key, w) && aligned(value, w) && aligned(k_cache, w) && aligned(v_cache, w) &&
+           a.key_stride_bytes % w == 0 && a.value_stride_bytes % w == 0 && a.row_bytes % w == 0;
+  };
+  while (vec > 1 && !fits(vec)) vec >>= 1;
+  cudaError_t e = dllm::launch_kv_copy(a, store, vec, num_sms_of_current_device(),
+                                       reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, store ? "store_kvcache launch" : "load_kvcache launch");
+  return DLLM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dllm_version(void) { return 100; }
+
+const char* dllm_last_error(void) { return g_last_error.c_str(); }
+
+int dllm_store_kvcache(const void* key, int64_t key_stride, const void* value, int64_t value_stride,
+                       void* k_cache, void* v_cache, const int32_t* slot_mapping, int64_t n_tokens,
+                       int64_t row_elems, int elem_bytes, int64_t num_slots, int32_t* err_flag,
+                       void* stream) {
+  return kv_copy_common(true, key, key_stride, value, value_stride, k_cache, v_cache, slot_mapping,
+                        n_tokens, row_elems, elem_bytes, num_slots, err_flag, stream);
+}
+
+int dllm_load_kvcache(void* key, int64_t key_stride, void* value, int64_t value_stride,
+                      const void* k_cache, const void* v_cache, const int32_t* slot_mapping,
+                      int64_t n_tokens, int64_t row_elems, int elem_bytes, int64_t num_slots,
+                      int32_t* err_flag, void* stream) {
+  return kv_copy_common(false, key, key_stride, value, value_stride, k_cache, v_cache,
+                        slot_mapping, n_tokens, row_elems, elem_bytes, num_slots, err_flag, stream);
+}
+
+int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                         const void* v, int64_t v_tok_stride, void* o, int64_t o_tok_stride,
+                         const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
+                         int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
+                         int num_kv_heads, int head_dim, float softmax_scale, int32_t* err_flag,
+                         void* stream) {
+  return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, nullptr, 0, nullptr, 0, o,
+                     o_tok_stride, cu_seqlens_q, cu_seqlens_k, nullptr, batch, max_seqlen_q,
+                     total_q, total_k, 0, num_heads, num_kv_heads, head_dim, softmax_scale,
+                     err_flag, stream);
+}
+
+int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, const void* k,
+                                int64_t k_tok_stride, const void* v, int64_t v_tok_stride,
+                                const void* kc, int64_t kc_tok_stride, const void* vc,
+                                int64_t vc_tok_stride, void* o, int64_t o_tok_stride,
+                                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                                const int32_t* cu_seqlens_c, int batch, int max_seqlen_q,
+                                int64_t total_q, int64_t total_k, int64_t total_c, int num_heads,
+                                int num_kv_heads, int head_dim, float softmax_scale,
+                                int32_t* err_flag, void* stream) {
+  if (cu_seqlens_c == nullptr) return fail(DLLM_ERR_INVALID_ARG, "cu_seqlens_c is null");
+  return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, kc, kc_tok_stride, vc,
+                     vc_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k, cu_seqlens_c,
+                     batch, max_seqlen_q, total_q, total_k, total_c, num_heads, num_kv_heads,
+                     head_dim, softmax_scale, err_flag, stream);
+}
+
+int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                         const void* v, int64_t v_tok_stride, const int32_t* seq_desc, int n_seqs,
+                         int max_klen, int num_heads, int num_kv_heads, int head_dim,
+                         int head_select, void* k_cache, void* v_cache, int64_t cache_tok_stride,
+                         int64_t num_slots, const int32_t* slots, int64_t* top_idx,
+                         int32_t* err_flag, void* stream) {
+  if (head_dim != 128)
+    return fail(DLLM_ERR_UNSUPPORTED, "head_dim %d not supported (only 128)", head_dim);
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0)
+    return fail(DLLM_ERR_UNSUPPORTED, "num_heads must be a positive multiple of num_kv_heads");
+  if (n_seqs < 0 || max_klen < 0) return fail(DLLM_ERR_INVALID_ARG, "negative size");
+  if (max_klen > 16384) return fail(DLLM_ERR_TOO_LARGE, "max_klen %d > 16384", max_klen);
+  if (n_seqs == 0 || max_klen == 0) return DLLM_OK;
+  if (!q || !k || !v || !seq_desc || !k_cache || !v_cache || !slots)
+    return fail(DLLM_ERR_INVALID_ARG, "null pointer");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(k_cache, 16) ||
+      !aligned(v_cache, 16) || q_tok_stride % 8 || k_tok_stride % 8 || v_tok_stride % 8 ||
+      cache_tok_stride % 8)
+    return fail(DLLM_ERR_ALIGNMENT, "q/k/v/cache must be 16-byte aligned with strides %% 8 == 0");
+  if (cache_tok_stride < (int64_t)num_kv_heads * 128)
+    return fail(DLLM_ERR_INVALID_ARG, "cache_tok_stride smaller than num_kv_heads*head_dim");
+  dllm::SelectArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k);
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v);
+  a.q_tok_stride = q_tok_stride;
+  a.k_tok_stride = k_tok_stride;
+  a.v_tok_stride = v_tok_stride;
+  a.seq_desc = seq_desc;
+  a.max_klen = max_klen;
+  a.Hq = num_heads;
+  a.Hkv = num_kv_heads;
+  a.group = num_heads / num_kv_heads;
+  a.sqrt_d = (float)sqrt((double)head_dim);
+  a.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache);
+  a.cache_tok_stride = cache_tok_stride;
+  a.num_slots = num_slots;
+  a.slots = slots;
+  a.top_idx = top_idx;
+  a.err = err_flag;
+  const size_t smem = dllm::select_kv_smem_bytes(head_select ? a.group : a.Hq, max_klen);
+  if (smem > 227 * 1024) return fail(DLLM_ERR_TOO_LARGE, "select_kv needs %zu B smem", smem);
+  cudaError_t e = dllm::launch_select_kv(a, head_select != 0, n_seqs,
+                                         reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "select_kv launch");
+  return DLLM_OK;
+}
+
+}  // extern "C"

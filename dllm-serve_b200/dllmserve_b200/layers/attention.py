@@ -1,0 +1,114 @@
+"""Drop-in ``Attention`` layer for diffusion LLMs on B200.
+
+Keeps the reference's module contract (dllmserve/layers/attention.py:95-119):
+``Attention(num_heads, head_dim, scale, num_kv_heads, causal=True)`` with the
+``k_cache`` / ``v_cache`` / ``layer_id`` attributes bound by the model runner,
+and ``forward(q, k, v) -> [N, num_heads * head_dim]`` reading the per-step
+``Context``. Also re-exports ``store_kvcache`` / ``load_kvcache`` with the
+reference's argument order and assertions (attention.py:33-92).
+
+The diffusion path (``context.is_diffusion``, attention.py:150-306) runs as
+  1. one scoring/top-k/store launch per ``head_select`` flavour for the
+     sequences in the "compute cache" state (state 1),
+  2. one gather of the cached rows of "reuse" sequences (state 2), and
+  3. one non-causal varlen attention launch over every sequence, whose keys
+     are [cached rows ; fresh rows] for state-2 sequences,
+with all per-sequence metadata built once per step (``StepPlan``).
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from .. import ops
+from ..engine.step_plan import build_step_plan, selection_arrays
+from ..utils import context as _context_mod
+
+# Where the layer reads the step context from. ``integration.install`` points
+# this at the reference package's ``get_context`` so a reference model runner
+# drives this layer unchanged.
+get_context = _context_mod.get_context
+
+store_kvcache = ops.store_kvcache
+load_kvcache = ops.load_kvcache
+
+_PLAN_ATTR = "_dllm_b200_plans"
+
+
+def _plan_for(ctx, q: torch.Tensor):
+    plans = getattr(ctx, _PLAN_ATTR, None)
+    if plans is None:
+        plans = {}
+        try:
+            setattr(ctx, _PLAN_ATTR, plans)
+        except AttributeError:  # a frozen context: rebuild per layer
+            pass
+    key = (q.device, q.shape[0])
+    plan = plans.get(key)
+    if plan is None:
+        plan = build_step_plan(ctx, q.device, q.shape[0])
+        plans[key] = plan
+    return plan
+
+
+class Attention(nn.Module):
+    def __init__(self, num_heads, head_dim, scale, num_kv_heads, causal=True):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.scale = scale
+        self.num_kv_heads = num_kv_heads
+        self.causal = causal
+        self.k_cache = self.v_cache = torch.tensor([])
+        self.layer_id = None
+        # top_idx of the last "compute cache" launch per head_select flavour
+        # (device int64); kept only when ``record_selection`` is set.
+        self.record_selection = False
+        self.last_selection: dict = {}
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        q = q.view(-1, self.num_heads, self.head_dim)
+        k = k.view(-1, self.num_kv_heads, self.head_dim)
+        v = v.view(-1, self.num_kv_heads, self.head_dim)
+        context = get_context()
+        if context.is_diffusion:
+            return self._diffusion_attention(q, k, v, context)
+        if self.k_cache.numel() and self.v_cache.numel():
+            store_kvcache(k, v, self.k_cache, self.v_cache, context.slot_mapping)
+        return self._regular_attention(q, k, v, context)
+
+    def _regular_attention(self, q, k, v, context):
+        """Non-diffusion path (attention.py:121-148). Only the non-causal,
+        non-paged prefill form exists on this path's kernels."""
+        if self.causal or not context.is_prefill or context.block_tables is not None:
+            raise NotImplementedError(
+                "dllmserve_b200 implements the diffusion (non-causal) attention path only")
+        o = ops.varlen_attention(q, k, v, context.cu_seqlens_q, context.cu_seqlens_k,
+                                 int(context.max_seqlen_q), self.scale)
+        return o.view(-1, self.num_heads * self.head_dim)
+
+    def _diffusion_attention(self, q, k, v, context):
+        plan = _plan_for(context, q)
+        dev = q.device
+        if self.record_selection:
+            self.last_selection = {}
+        for head_select in (True, False):
+            arrs = selection_arrays(plan, head_select, self.num_kv_heads, dev)
+            if arrs is None:
+                continue
+            desc, slots, max_klen, idx_total = arrs
+            top_idx = None
+            if self.record_selection:
+                top_idx = torch.empty(idx_total, dtype=torch.int64, device=dev)
+                self.last_selection[head_select] = top_idx
+            ops.select_kv_store(q, k, v, desc, max_klen, head_select,
+                                self.k_cache, self.v_cache, slots, top_idx)
+        out = torch.empty((q.shape[0], self.num_heads, self.head_dim), dtype=q.dtype, device=dev)
+        if plan.total_c > 0:
+            kc, vc = plan.cached_buffers(self.num_kv_heads, self.head_dim, k.dtype, dev)
+            load_kvcache(kc, vc, self.k_cache, self.v_cache, plan.slots_c)
+            ops.varlen_attention(q, k, v, plan.cu, plan.cu, plan.max_rows, self.scale,
+                                 k_cached=kc, v_cached=vc, cu_seqlens_c=plan.cu_c, out=out)
+        else:
+            ops.varlen_attention(q, k, v, plan.cu, plan.cu, plan.max_rows, self.scale, out=out)
+        return out.view(-1, self.num_heads * self.head_dim)

@@ -1,0 +1,248 @@
+"""Torch-facing wrappers of the native attention-path ops.
+
+Every op validates shapes/dtypes on the host (no device reads), then calls
+the C ABI on the tensors' device with ``torch.cuda.current_stream()``.
+The tensors must live on a CUDA device; there is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _native
+
+_STATUS: dict[int, torch.Tensor] = {}
+
+# Number of native kernel launches issued through this module (benchmarks
+# report the count inside their timed region).
+LAUNCHES = [0]
+
+
+def device_status_word(device: torch.device) -> torch.Tensor:
+    """The int32 device word the kernels report DLLM_DEV_* codes into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = t
+    return t
+
+
+def read_device_status(device: torch.device, reset: bool = True) -> int:
+    """Synchronising read of the device status word (tests / debug only)."""
+    t = device_status_word(device)
+    v = int(t.item())
+    if reset and v:
+        t.zero_()
+    return v
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if t.device.type != "cuda":
+            raise ValueError("dllmserve_b200 ops need CUDA tensors (there is no CPU path)")
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def _stream_ptr() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# KV cache (attention.py:33-50, 77-92)
+# ---------------------------------------------------------------------------
+def store_kvcache(key, value, k_cache, v_cache, slot_mapping):
+    """cache[slot_mapping[i]] <- key[i], value[i]. Same argument order and
+    assertions as the reference's ``store_kvcache`` (attention.py:33-50)."""
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert k_cache.stride(1) == D and v_cache.stride(1) == D
+    assert slot_mapping.numel() == N
+    _kv_copy(True, key, value, k_cache, v_cache, slot_mapping, D)
+
+
+def load_kvcache(key, value, k_cache, v_cache, slot_mapping):
+    """key[i], value[i] <- cache[slot_mapping[i]] (attention.py:77-92)."""
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert k_cache.stride(1) == D and v_cache.stride(1) == D
+    assert slot_mapping.numel() == N
+    _kv_copy(False, key, value, k_cache, v_cache, slot_mapping, D)
+
+
+def _kv_copy(store, key, value, k_cache, v_cache, slot_mapping, D):
+    N = key.shape[0]
+    if N == 0:
+        return
+    dev = _require_cuda(key, value, k_cache, v_cache, slot_mapping)
+    if key.dtype != k_cache.dtype or value.dtype != v_cache.dtype or key.dtype != value.dtype:
+        raise ValueError("key/value and cache dtypes must match")
+    if slot_mapping.dtype != torch.int32:
+        raise ValueError("slot_mapping must be int32")
+    if not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be contiguous")
+    # a cache slot is D contiguous elements, slots D apart (asserted above)
+    num_slots = k_cache.numel() // D
+    if v_cache.numel() // D != num_slots:
+        raise ValueError("k_cache and v_cache hold different numbers of slots")
+    lib = _native.lib()
+    fn = lib.dllm_store_kvcache if store else lib.dllm_load_kvcache
+    with torch.cuda.device(dev):
+        rc = fn(
+            key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+            k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr(),
+            N, D, key.element_size(), num_slots,
+            device_status_word(dev).data_ptr(), _stream_ptr(),
+        )
+    _native.check(rc, "store_kvcache" if store else "load_kvcache")
+    LAUNCHES[0] += 1
+
+
+# ---------------------------------------------------------------------------
+# Attention (attention.py:289-299, 235-265)
+# ---------------------------------------------------------------------------
+def _check_rows(name, t, heads, head_dim):
+    if t.dim() != 3 or t.shape[1] != heads or t.shape[2] != head_dim:
+        raise ValueError(f"{name} must be [tokens, {heads}, {head_dim}], got {tuple(t.shape)}")
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bfloat16")
+    if t.stride(2) != 1 or t.stride(1) != head_dim:
+        raise ValueError(f"{name} must have contiguous heads (strides [*, {head_dim}, 1])")
+
+
+def varlen_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    cu_seqlens_k: torch.Tensor,
+    max_seqlen_q: int,
+    softmax_scale: float | None = None,
+    *,
+    k_cached: torch.Tensor | None = None,
+    v_cached: torch.Tensor | None = None,
+    cu_seqlens_c: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Non-causal varlen attention (bf16). With ``k_cached``/``v_cached``/
+    ``cu_seqlens_c`` each sequence attends to [cached rows ; fresh rows]."""
+    Hq, D = q.shape[1], q.shape[2]
+    Hkv = k.shape[1]
+    _check_rows("q", q, Hq, D)
+    _check_rows("k", k, Hkv, D)
+    _check_rows("v", v, Hkv, D)
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    dev = _require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k)
+    for name, c in (("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+        if c.dtype != torch.int32 or not c.is_contiguous():
+            raise ValueError(f"{name} must be contiguous int32")
+    B = cu_seqlens_q.numel() - 1
+    if cu_seqlens_k.numel() != B + 1:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k sizes differ")
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    else:
+        _check_rows("out", out, Hq, D)
+        if out.shape[0] != q.shape[0]:
+            raise ValueError("out must have as many rows as q")
+    lib = _native.lib()
+    status = device_status_word(dev).data_ptr()
+    with torch.cuda.device(dev):
+        if k_cached is None:
+            rc = lib.dllm_attn_varlen_fwd(
+                q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
+                B, int(max_seqlen_q), q.shape[0], k.shape[0], Hq, Hkv, D, float(softmax_scale),
+                status, _stream_ptr(),
+            )
+        else:
+            _check_rows("k_cached", k_cached, Hkv, D)
+            _check_rows("v_cached", v_cached, Hkv, D)
+            _require_cuda(q, k_cached, v_cached, cu_seqlens_c)
+            if cu_seqlens_c.dtype != torch.int32 or cu_seqlens_c.numel() != B + 1:
+                raise ValueError("cu_seqlens_c must be int32 [batch+1]")
+            if v_cached.shape[0] != k_cached.shape[0]:
+                raise ValueError("k_cached and v_cached rows differ")
+            rc = lib.dllm_attn_varlen_cached_fwd(
+                q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                k_cached.data_ptr(), k_cached.stride(0), v_cached.data_ptr(), v_cached.stride(0),
+                out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
+                cu_seqlens_c.data_ptr(), B, int(max_seqlen_q), q.shape[0], k.shape[0],
+                k_cached.shape[0], Hq, Hkv, D, float(softmax_scale), status, _stream_ptr(),
+            )
+    _native.check(rc, "varlen_attention")
+    if B > 0 and q.shape[0] > 0:
+        LAUNCHES[0] += 1
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Scoring + top-k + gather + store (attention.py:308-342, 344-413, 204-233)
+# ---------------------------------------------------------------------------
+def select_kv_store(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    seq_desc: torch.Tensor,
+    max_klen: int,
+    head_select: bool,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    slots: torch.Tensor,
+    top_idx: torch.Tensor | None = None,
+) -> None:
+    """Score candidates, pick the top n_keep per sequence (per KV head with
+    ``head_select``), write their K/V rows into ``slots`` of the cache and,
+    if given, the chosen candidate indices into ``top_idx`` (int64)."""
+    Hq, D = q.shape[1], q.shape[2]
+    Hkv = k.shape[1]
+    _check_rows("q", q, Hq, D)
+    _check_rows("k", k, Hkv, D)
+    _check_rows("v", v, Hkv, D)
+    dev = _require_cuda(q, k, v, seq_desc, k_cache, v_cache, slots)
+    if seq_desc.dtype != torch.int32 or seq_desc.dim() != 2 or seq_desc.shape[1] != _native.SEQ_DESC_INTS:
+        raise ValueError("seq_desc must be int32 [n_seqs, 8]")
+    if not seq_desc.is_contiguous() or slots.dtype != torch.int32 or not slots.is_contiguous():
+        raise ValueError("seq_desc and slots must be contiguous int32")
+    if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise ValueError("caches must be bfloat16")
+    row = Hkv * D
+    if k_cache.stride(-1) != 1 or k_cache.numel() % row != 0 or v_cache.numel() != k_cache.numel():
+        raise ValueError("caches must be contiguous rows of num_kv_heads*head_dim")
+    if top_idx is not None:
+        _require_cuda(q, top_idx)
+        if top_idx.dtype != torch.int64 or not top_idx.is_contiguous():
+            raise ValueError("top_idx must be contiguous int64")
+    lib = _native.lib()
+    with torch.cuda.device(dev):
+        rc = lib.dllm_select_kv_store(
+            q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+            seq_desc.data_ptr(), seq_desc.shape[0], int(max_klen), Hq, Hkv, D, int(bool(head_select)),
+            k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row, slots.data_ptr(),
+            _ptr(top_idx), device_status_word(dev).data_ptr(), _stream_ptr(),
+        )
+    _native.check(rc, "select_kv_store")
+    if seq_desc.shape[0] > 0 and max_klen > 0:
+        LAUNCHES[0] += 1
+
+
+def attention_flops(q_lens, k_lens, num_heads: int, head_dim: int) -> float:
+    """4 * sum(Lq * Lk) * Hq * D (non-causal; QK^T and PV)."""
+    return 4.0 * float(sum(int(a) * int(b) for a, b in zip(q_lens, k_lens))) * num_heads * head_dim
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

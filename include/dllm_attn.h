@@ -1,0 +1,168 @@
+/*
+ * dllm_attn.h - C ABI of the B200 (sm_100a) attention-path library
+ * (libdllm_attn.so) for diffusion-LLM serving.
+ *
+ * Each entry point replaces one piece of the reference's per-denoising-step
+ * attention path (chosen-ox/dLLM-Serve, dllmserve/layers/attention.py):
+ *
+ *   dllm_store_kvcache        <- store_kvcache + store_kvcache_kernel   (attention.py:11-50)
+ *   dllm_load_kvcache         <- load_kvcache + load_kvcache_kernel     (attention.py:53-92)
+ *   dllm_attn_varlen_fwd      <- flash_attn_varlen_func(..., causal=False) (attention.py:289-299)
+ *   dllm_attn_varlen_cached_fwd
+ *                             <- reuse-state K/V assembly + varlen call (attention.py:235-299):
+ *                                keys are [cached selected rows ; fresh block rows]
+ *   dllm_select_kv_store      <- _select_important_head_kv (attention.py:344-413) or
+ *                                _select_important_kv (attention.py:308-342), followed by
+ *                                the k_prefix_suffix[idx] gather and store_kvcache of the
+ *                                selected rows (attention.py:204-233)
+ *
+ * Conventions
+ *   - Every pointer except `err_flag`/`top_idx` arguments documented as optional is a
+ *     device pointer owned by the caller. The library never allocates or frees memory,
+ *     never synchronises the stream and never reads device data on the host, so every
+ *     call can be captured in a CUDA graph.
+ *   - `stream` is a cudaStream_t passed as void*. NULL means the legacy default stream.
+ *   - Strides are in ELEMENTS unless the name ends in `_bytes`.
+ *   - bf16 tensors are laid out [tokens, heads, head_dim] with head_dim contiguous and
+ *     heads packed (head stride == head_dim); the token stride is free (views of a fused
+ *     qkv projection are accepted) but must be a multiple of 8 elements.
+ *   - Return value: DLLM_OK or one of the DLLM_ERR_* codes; dllm_last_error() gives a
+ *     one-line message for the calling thread.
+ *   - `err_flag` (optional, int32 device word) receives a device-side status: the first
+ *     nonzero DLLM_DEV_* code seen by any kernel thread. The caller clears and reads it.
+ */
+#ifndef DLLM_ATTN_H_
+#define DLLM_ATTN_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DLLM_API __attribute__((visibility("default")))
+#else
+#define DLLM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* host-side return codes */
+#define DLLM_OK 0
+#define DLLM_ERR_INVALID_ARG 1   /* null pointer, negative size, inconsistent sizes */
+#define DLLM_ERR_UNSUPPORTED 2   /* head_dim / head ratio not supported */
+#define DLLM_ERR_ALIGNMENT 3     /* pointer or stride not aligned for vector/TMA access */
+#define DLLM_ERR_TOO_LARGE 4     /* a size beyond the kernel's limit */
+#define DLLM_ERR_CUDA 5          /* CUDA launch / driver error */
+
+/* device-side status codes written to err_flag */
+#define DLLM_DEV_SLOT_OUT_OF_RANGE 1
+#define DLLM_DEV_WAIT_TIMEOUT 2
+#define DLLM_DEV_BAD_SEQUENCE 3
+
+/* Library version (major*10000 + minor*100 + patch). */
+DLLM_API int dllm_version(void);
+
+/* Message describing the last failing call on this thread ("" if none). */
+DLLM_API const char* dllm_last_error(void);
+
+/*
+ * cache[slot_mapping[i]] <- key[i], value[i]  for i in [0, n_tokens)
+ * Replaces store_kvcache (attention.py:33-50) and its Triton kernel (:11-30).
+ * A cache row (one slot) holds `row_elems` contiguous elements (= num_kv_heads*head_dim),
+ * `elem_bytes` wide. key/value row i starts at key + i*key_stride elements.
+ * Slots < 0 are skipped; slots >= num_slots are skipped and flag
+ * DLLM_DEV_SLOT_OUT_OF_RANGE in err_flag.
+ */
+DLLM_API int dllm_store_kvcache(const void* key, int64_t key_stride, const void* value,
+                       int64_t value_stride, void* k_cache, void* v_cache,
+                       const int32_t* slot_mapping, int64_t n_tokens, int64_t row_elems,
+                       int elem_bytes, int64_t num_slots, int32_t* err_flag, void* stream);
+
+/*
+ * key[i], value[i] <- cache[slot_mapping[i]]  for i in [0, n_tokens)
+ * Replaces load_kvcache (attention.py:77-92) and its Triton kernel (:53-74).
+ * Out-of-range slots produce zero rows (negative: silently; >= num_slots: also flag).
+ */
+DLLM_API int dllm_load_kvcache(void* key, int64_t key_stride, void* value, int64_t value_stride,
+                      const void* k_cache, const void* v_cache, const int32_t* slot_mapping,
+                      int64_t n_tokens, int64_t row_elems, int elem_bytes, int64_t num_slots,
+                      int32_t* err_flag, void* stream);
+
+/*
+ * Non-causal varlen attention, bf16 in/out, fp32 accumulation:
+ *   o[q rows of seq b] = softmax(Q_b K_b^T * softmax_scale) V_b
+ * Replaces flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+ * max_seqlen_k, softmax_scale, causal=False) as called at attention.py:289-299.
+ * q: [total_q, num_heads, head_dim]; k, v: [total_k, num_kv_heads, head_dim];
+ * o: [total_q, num_heads, head_dim]. cu_seqlens_*: int32 [batch+1], device.
+ * max_seqlen_q must be >= every query length (it sizes the grid). GQA when
+ * num_heads is a multiple of num_kv_heads. head_dim must be 128.
+ */
+DLLM_API int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                         const void* v, int64_t v_tok_stride, void* o, int64_t o_tok_stride,
+                         const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
+                         int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
+                         int num_kv_heads, int head_dim, float softmax_scale, int32_t* err_flag,
+                         void* stream);
+
+/*
+ * As dllm_attn_varlen_fwd, but the keys/values of sequence b are the
+ * concatenation [cached rows cu_seqlens_c[b]..cu_seqlens_c[b+1] of kc/vc ;
+ * fresh rows cu_seqlens_k[b]..cu_seqlens_k[b+1] of k/v], without materialising
+ * the concatenation. Replaces the reuse-state assembly of attention.py:235-265
+ * (zeros + load_kvcache + torch.cat) feeding the varlen call at :289-299.
+ * kc, vc: [total_c, num_kv_heads, head_dim] with token strides kc_tok_stride/vc_tok_stride.
+ */
+DLLM_API int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, const void* k,
+                                int64_t k_tok_stride, const void* v, int64_t v_tok_stride,
+                                const void* kc, int64_t kc_tok_stride, const void* vc,
+                                int64_t vc_tok_stride, void* o, int64_t o_tok_stride,
+                                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                                const int32_t* cu_seqlens_c, int batch, int max_seqlen_q,
+                                int64_t total_q, int64_t total_k, int64_t total_c,
+                                int num_heads, int num_kv_heads, int head_dim,
+                                float softmax_scale, int32_t* err_flag, void* stream);
+
+/*
+ * Per-sequence descriptor for dllm_select_kv_store: 8 int32 values per sequence.
+ *   [0] tok_start   row of the sequence's first token in q/k/v
+ *   [1] seq_len     tokens of the sequence in q/k/v (L)
+ *   [2] blk_start   start of the current diffusion block, relative to tok_start
+ *   [3] blk_len     tokens in the block; candidates are the other L-blk_len tokens
+ *   [4] n_keep      rows to keep: min(max(1, int(Klen*retention_ratio)), Klen), 0 if Klen==0
+ *   [5] slot_off    offset of this sequence's n_keep slots in `slots`
+ *   [6] idx_off     offset of this sequence's indices in `top_idx` (elements)
+ *   [7] pool_kernel max-pool window over candidate scores (<=1: none)
+ */
+#define DLLM_SEQ_DESC_INTS 8
+
+/*
+ * Importance scoring + top-k selection + gather + KV-cache store, for every
+ * sequence of the step that is in the "compute cache" state.
+ *   q_avg[h]   = mean of the block's query rows (fp32)
+ *   head_select != 0 (attention.py:344-413): per KV head h,
+ *       s[h,c] = max over the head's query group g of q_avg[g].k[c,h] / sqrt(head_dim)
+ *     else (attention.py:308-342): one shared ranking,
+ *       s[c]   = sum over all query heads g of q_avg[g].k[c, g/group] / sqrt(head_dim)
+ *   s <- max_pool1d(s, pool_kernel, stride 1, padding pool_kernel/2)[:Klen]
+ *   idx = the n_keep largest scores, ordered by descending score, ties by ascending
+ *         candidate index
+ *   k_cache[slots[j]] (head h, or all heads) <- k[candidate idx[j]], same for v.
+ * Candidates are the sequence's tokens outside [blk_start, blk_start+blk_len), in order.
+ * top_idx (optional, int64, device): per sequence [num_kv_heads, n_keep] (head_select)
+ * or [n_keep] at idx_off. max_klen must be >= every Klen and <= 16384.
+ * `cache_tok_stride` is the element stride between cache slots (num_kv_heads*head_dim
+ * for the reference layout).
+ */
+DLLM_API int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                         const void* v, int64_t v_tok_stride, const int32_t* seq_desc,
+                         int n_seqs, int max_klen, int num_heads, int num_kv_heads, int head_dim,
+                         int head_select, void* k_cache, void* v_cache, int64_t cache_tok_stride,
+                         int64_t num_slots, const int32_t* slots, int64_t* top_idx,
+                         int32_t* err_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DLLM_ATTN_H_ */

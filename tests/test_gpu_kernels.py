@@ -1,0 +1,322 @@
+"""GPU parity tests of the native kernels against the CPU oracle.
+
+Tolerances (from the benchmark spec): attention outputs in bf16 vs the fp32
+oracle within max-abs 2e-2 and mean-abs 2e-3; KV-cache contents bit-exact;
+selected indices bit-exact (same tie rule: descending score, ascending index).
+"""
+import numpy as np
+import pytest
+import torch
+
+import inputs as I
+from oracle import attention_ref as R
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    d = torch.device("cuda:0")
+    torch.cuda.set_device(d)
+    from dllmserve_b200 import _native
+
+    _native.lib()
+    return d
+
+
+def _ops():
+    from dllmserve_b200 import ops
+
+    return ops
+
+
+def _status_clear(dev):
+    assert _ops().read_device_status(dev) == 0
+
+
+def _cu(lens):
+    c = [0]
+    for L in lens:
+        c.append(c[-1] + L)
+    return c
+
+
+def _check_attn(out_gpu, ref, what=""):
+    err = (out_gpu.float().cpu() - ref).abs()
+    assert torch.isfinite(out_gpu.float()).all(), f"{what}: non-finite output"
+    assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS, (
+        f"{what}: max {err.max().item():.3e} mean {err.mean().item():.3e}")
+
+
+# ---------------------------------------------------------------------------
+# KV cache store / load
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("n,hkv", [(1, 32), (7, 4), (300, 32), (1000, 1), (4097, 8)])
+def test_store_kvcache_bit_exact(dev, n, hkv):
+    g = I.gen(n + hkv)
+    D = 128
+    pages = (n + 255) // 256 + 3
+    key = I.normal(g, (n, hkv, D)).to(torch.bfloat16)
+    val = I.normal(g, (n, hkv, D)).to(torch.bfloat16)
+    slots = torch.randperm(pages * 256, generator=g)[:n].to(torch.int32)
+    canary = torch.full((pages, 256, hkv, D), 7.0, dtype=torch.bfloat16)
+    kc_ref, vc_ref = canary.clone(), canary.clone()
+    R.store_kvcache(key, val, kc_ref, vc_ref, slots)
+    kc, vc = canary.to(dev), canary.to(dev)
+    _ops().store_kvcache(key.to(dev), val.to(dev), kc, vc, slots.to(dev))
+    torch.cuda.synchronize()
+    assert torch.equal(kc.cpu(), kc_ref) and torch.equal(vc.cpu(), vc_ref)
+    _status_clear(dev)
+
+
+def test_store_kvcache_strided_rows(dev):
+    """key/value as column slices of a fused qkv buffer (token stride > row)."""
+    g = I.gen(5)
+    n, hq, hkv, D = 333, 8, 2, 128
+    qkv = I.normal(g, (n, (hq + 2 * hkv) * D)).to(torch.bfloat16).to(dev)
+    k = qkv[:, hq * D:(hq + hkv) * D].view(n, hkv, D)
+    v = qkv[:, (hq + hkv) * D:].view(n, hkv, D)
+    slots = torch.randperm(512, generator=g)[:n].to(torch.int32)
+    kc = torch.zeros(2, 256, hkv, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    _ops().store_kvcache(k, v, kc, vc, slots.to(dev))
+    kr, vr = torch.zeros(2, 256, hkv, D, dtype=torch.bfloat16), torch.zeros(2, 256, hkv, D, dtype=torch.bfloat16)
+    R.store_kvcache(k.cpu(), v.cpu(), kr, vr, slots)
+    assert torch.equal(kc.cpu(), kr) and torch.equal(vc.cpu(), vr)
+
+
+def test_load_kvcache_bit_exact(dev):
+    g = I.gen(9)
+    hkv, D, pages, n = 4, 128, 6, 900
+    kc = I.normal(g, (pages, 256, hkv, D)).to(torch.bfloat16)
+    vc = I.normal(g, (pages, 256, hkv, D)).to(torch.bfloat16)
+    slots = torch.randint(0, pages * 256, (n,), generator=g).to(torch.int32)
+    k_ref, v_ref = R.load_kvcache(kc, vc, slots, hkv, D)
+    k = torch.full((n, hkv, D), float("nan"), dtype=torch.bfloat16, device=dev)
+    v = torch.full_like(k, float("nan"))
+    _ops().load_kvcache(k, v, kc.to(dev), vc.to(dev), slots.to(dev))
+    assert torch.equal(k.cpu(), k_ref) and torch.equal(v.cpu(), v_ref)
+
+
+def test_slot_edge_cases(dev):
+    """Negative slots are skipped; slots past the cache are skipped and flagged."""
+    hkv, D = 2, 128
+    key = torch.ones(3, hkv, D, dtype=torch.bfloat16, device=dev)
+    kc = torch.zeros(1, 256, hkv, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    ops = _ops()
+    ops.store_kvcache(key, key, kc, vc, torch.tensor([-1, 5, 256], dtype=torch.int32, device=dev))
+    torch.cuda.synchronize()
+    assert ops.read_device_status(dev) == 1
+    ref = torch.zeros(256, hkv, D, dtype=torch.bfloat16)
+    ref[5] = 1
+    assert torch.equal(kc.cpu().view(256, hkv, D), ref)
+    # empty store is a no-op
+    ops.store_kvcache(key[:0], key[:0], kc, vc, torch.zeros(0, dtype=torch.int32, device=dev))
+    _status_clear(dev)
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+SMALL_LENS = [[1], [2], [31], [33], [127], [128], [129], [255], [256], [257], [300], [513],
+              [1, 2, 3], [129, 7, 256, 1]]
+
+
+@pytest.mark.parametrize("lens", SMALL_LENS, ids=[str(x) for x in SMALL_LENS])
+@pytest.mark.parametrize("hq,hkv", [(4, 4), (7, 1), (8, 2)])
+def test_attention_small(dev, lens, hq, hkv):
+    g = I.gen(sum(lens) * 31 + hq)
+    D, N = 128, sum(lens)
+    q, k, v = I.normal(g, (N, hq, D)), I.normal(g, (N, hkv, D)), I.normal(g, (N, hkv, D))
+    cu = _cu(lens)
+    ref = R.varlen_attention(q, k, v, cu, cu, D ** -0.5)
+    cu_d = torch.tensor(cu, dtype=torch.int32, device=dev)
+    out = torch.full((N, hq, D), float("nan"), dtype=torch.bfloat16, device=dev)
+    _ops().varlen_attention(q.to(dev, torch.bfloat16), k.to(dev, torch.bfloat16),
+                            v.to(dev, torch.bfloat16), cu_d, cu_d, max(lens), D ** -0.5, out=out)
+    torch.cuda.synchronize()
+    _check_attn(out, ref, f"lens={lens} hq={hq} hkv={hkv}")
+    _status_clear(dev)
+
+
+def test_attention_separate_q_and_k_lengths(dev):
+    """Lq != Lk per sequence (flash_attn_varlen_func semantics)."""
+    g = I.gen(77)
+    D, hq, hkv = 128, 4, 2
+    lq, lk = [5, 200, 130], [300, 1, 129]
+    q = I.normal(g, (sum(lq), hq, D))
+    k, v = I.normal(g, (sum(lk), hkv, D)), I.normal(g, (sum(lk), hkv, D))
+    ref = R.varlen_attention(q, k, v, _cu(lq), _cu(lk), 0.1)
+    out = _ops().varlen_attention(
+        q.to(dev, torch.bfloat16), k.to(dev, torch.bfloat16), v.to(dev, torch.bfloat16),
+        torch.tensor(_cu(lq), dtype=torch.int32, device=dev),
+        torch.tensor(_cu(lk), dtype=torch.int32, device=dev), max(lq), 0.1)
+    _check_attn(out, ref)
+
+
+def test_attention_fused_qkv_views(dev):
+    """q/k/v as strided views of one fused projection output."""
+    g = I.gen(78)
+    D, hq, hkv, lens = 128, 8, 2, [100, 250]
+    N = sum(lens)
+    qkv = I.normal(g, (N, (hq + 2 * hkv) * D))
+    q = qkv[:, :hq * D].reshape(N, hq, D)
+    k = qkv[:, hq * D:(hq + hkv) * D].reshape(N, hkv, D)
+    v = qkv[:, (hq + hkv) * D:].reshape(N, hkv, D)
+    ref = R.varlen_attention(q, k, v, _cu(lens), _cu(lens), D ** -0.5)
+    qd = qkv.to(dev, torch.bfloat16)
+    cu = torch.tensor(_cu(lens), dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(qd[:, :hq * D].view(N, hq, D),
+                                  qd[:, hq * D:(hq + hkv) * D].view(N, hkv, D),
+                                  qd[:, (hq + hkv) * D:].view(N, hkv, D), cu, cu, max(lens))
+    _check_attn(out, ref)
+
+
+def test_attention_large_logits(dev):
+    """Rows whose max moves a lot across KV tiles exercise the rescaling path."""
+    g = I.gen(79)
+    D, H, L = 128, 2, 700
+    q = I.normal(g, (L, H, D)) * 3
+    k = I.normal(g, (L, H, D))
+    k[600:] *= 4  # the largest logits arrive in the last tiles
+    v = I.normal(g, (L, H, D))
+    q, k = q.to(torch.bfloat16).float(), k.to(torch.bfloat16).float()
+    ref = R.varlen_attention(q, k, v, [0, L], [0, L], D ** -0.5)
+    cu = torch.tensor([0, L], dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(q.to(dev, torch.bfloat16), k.to(dev, torch.bfloat16),
+                                  v.to(dev, torch.bfloat16), cu, cu, L)
+    _check_attn(out, ref)
+
+
+@pytest.mark.parametrize("hq,hkv", [(4, 4), (7, 1)])
+def test_attention_cached_segments(dev, hq, hkv):
+    """keys = [cached rows ; fresh rows] per sequence (the reuse state)."""
+    g = I.gen(80 + hq)
+    D = 128
+    lq = [32, 32, 17, 200]
+    lc = [304, 0, 129, 1]
+    q = I.normal(g, (sum(lq), hq, D))
+    k, v = I.normal(g, (sum(lq), hkv, D)), I.normal(g, (sum(lq), hkv, D))
+    kc, vc = I.normal(g, (sum(lc), hkv, D)), I.normal(g, (sum(lc), hkv, D))
+    ref = R.varlen_attention(q, k, v, _cu(lq), _cu(lq), D ** -0.5, kc, vc, _cu(lc))
+    t = lambda x: x.to(dev, torch.bfloat16)
+    cq = torch.tensor(_cu(lq), dtype=torch.int32, device=dev)
+    cc = torch.tensor(_cu(lc), dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(t(q), t(k), t(v), cq, cq, max(lq), D ** -0.5,
+                                  k_cached=t(kc), v_cached=t(vc), cu_seqlens_c=cc)
+    _check_attn(out, ref)
+    _status_clear(dev)
+
+
+def test_attention_c2_full_size_sampled(dev):
+    """Config-2 shapes (B=16, L in [384,1152], 32 MHA heads): every output
+    row finite; a sample of (sequence, head) pairs checked against the oracle."""
+    import bench
+
+    lens = bench.workload_lengths()
+    D, H = 128, 32
+    N = sum(lens)
+    gd = torch.Generator(device=dev).manual_seed(5)
+    q = torch.randn(N, H, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    k = torch.randn(N, H, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    v = torch.randn(N, H, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    cu = _cu(lens)
+    cud = torch.tensor(cu, dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(q, k, v, cud, cud, max(lens))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    for b in (0, 7, 15):
+        for h in (0, 13, 31):
+            s0, s1 = cu[b], cu[b + 1]
+            ref = R.sdpa_seq(q[s0:s1, h:h + 1].cpu(), k[s0:s1, h:h + 1].cpu(),
+                             v[s0:s1, h:h + 1].cpu(), D ** -0.5)
+            _check_attn(out[s0:s1, h:h + 1], ref, f"seq {b} head {h}")
+    _status_clear(dev)
+
+
+def test_attention_rejects_bad_args(dev):
+    ops = _ops()
+    q = torch.zeros(4, 2, 64, dtype=torch.bfloat16, device=dev)
+    cu = torch.tensor([0, 4], dtype=torch.int32, device=dev)
+    with pytest.raises(NotImplementedError):
+        ops.varlen_attention(q, q, q, cu, cu, 4)
+    q = torch.zeros(4, 3, 128, dtype=torch.bfloat16, device=dev)
+    k = torch.zeros(4, 2, 128, dtype=torch.bfloat16, device=dev)
+    with pytest.raises(NotImplementedError):
+        ops.varlen_attention(q, k, k, cu, cu, 4)
+
+
+# ---------------------------------------------------------------------------
+# scoring + top-k + store
+# ---------------------------------------------------------------------------
+SEL_CASES = [
+    # (hq, hkv, head_select, pool, ratio, seqs[(L, blk_start, blk_len)])
+    (4, 4, True, 3, 0.5, [(96, 64, 32), (134, 70, 32), (33, 1, 32)]),
+    (7, 1, True, 3, 0.5, [(640, 512, 32), (97, 65, 32)]),
+    (28, 4, True, 3, 0.5, [(704, 448, 32)]),
+    (8, 2, False, 3, 0.5, [(77, 45, 32), (154, 90, 32)]),
+    (32, 32, False, 5, 0.25, [(300, 100, 32)]),
+    (4, 4, True, 1, 0.5, [(200, 50, 32)]),
+    (4, 4, True, 4, 0.5, [(200, 50, 32)]),
+    (4, 2, True, 3, 0.0, [(100, 10, 32)]),
+    (4, 2, True, 3, 1.0, [(100, 10, 32)]),
+    (32, 32, True, 3, 0.25, [(4608, 4096, 32)]),
+]
+
+
+@pytest.mark.parametrize("case", SEL_CASES, ids=[f"c{i}" for i in range(len(SEL_CASES))])
+def test_select_kv_store_bit_exact(dev, case):
+    hq, hkv, hs, pool, ratio, seqs = case
+    D = 128
+    g = I.gen(hq * 100 + len(seqs))
+    N = sum(L for L, _, _ in seqs)
+    q, k, v = I.grid(g, (N, hq, D)), I.grid(g, (N, hkv, D)), I.grid(g, (N, hkv, D))
+    n_keeps = [R.num_keep(L - bl, ratio) for L, _, bl in seqs]
+    pages = sum((n + 255) // 256 for n in n_keeps) + 2
+    slots_list, off = [], 0
+    order = torch.randperm(pages, generator=g).tolist()
+    for n in n_keeps:
+        npg = (n + 255) // 256
+        lst = []
+        for j, p in enumerate(order[off:off + npg]):
+            lst.extend(range(p * 256, p * 256 + min(256, n - j * 256)))
+        off += npg
+        slots_list.append(torch.tensor(lst, dtype=torch.int32))
+    kc_ref = torch.zeros(pages, 256, hkv, D)
+    vc_ref = torch.zeros(pages, 256, hkv, D)
+    ref_idx = []
+    desc, row, slot_off, idx_off = [], 0, 0, 0
+    for (L, b0, bl), n, sl in zip(seqs, n_keeps, slots_list):
+        blk = torch.arange(row + b0, row + b0 + bl)
+        allr = torch.arange(row, row + L)
+        ps = allr[~torch.isin(allr, blk)]
+        if hs:
+            idx, ks, vs = R.select_important_head_kv(q[blk], k[ps], v[ps], hq, hkv, pool, ratio)
+        else:
+            idx = R.select_important_kv(q[blk], k[ps], hq, hkv, pool, ratio)
+            ks, vs = k[ps][torch.from_numpy(idx)], v[ps][torch.from_numpy(idx)]
+        R.store_kvcache(ks, vs, kc_ref, vc_ref, sl)
+        ref_idx.append(idx)
+        desc.append([row, L, b0, bl, n, slot_off, idx_off, pool])
+        row += L
+        slot_off += n
+        idx_off += n * (hkv if hs else 1)
+    t = lambda x: x.to(dev, torch.bfloat16)
+    kc = torch.zeros(pages, 256, hkv, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    top = torch.full((idx_off,), -1, dtype=torch.int64, device=dev)
+    _ops().select_kv_store(t(q), t(k), t(v), torch.tensor(desc, dtype=torch.int32, device=dev),
+                           max(L - bl for L, _, bl in seqs), hs, kc, vc,
+                           torch.cat(slots_list).to(dev), top)
+    torch.cuda.synchronize()
+    _status_clear(dev)
+    top = top.cpu().numpy()
+    for d, ri in zip(desc, ref_idx):
+        n = d[4]
+        got = top[d[6]:d[6] + n * (hkv if hs else 1)]
+        assert np.array_equal(got.reshape(ri.shape), ri)
+    assert torch.equal(kc.cpu().float(), kc_ref) and torch.equal(vc.cpu().float(), vc_ref)
