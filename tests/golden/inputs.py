@@ -2,10 +2,12 @@
 
 Two value families, both exactly representable in bf16:
   * ``normal``: N(0, 1) rounded to bf16.
-  * ``grid``:   integers in [-64, 64) times 2^-4. Dot products of up to 128
-    terms, means over power-of-two blocks and sums over heads are then exact
-    in fp32 whatever the summation order, so importance scores (and with them
-    the top-k selection) are bit-identical across implementations.
+  * ``grid``:   integers in [-32, 32) times 2^-5 (values in [-1, 1), the
+    scale of N(0,1) data, so the bf16 attention tolerances apply as stated).
+    Dot products of up to 128 terms, means over power-of-two blocks and sums
+    over heads are then exact in fp32 whatever the summation order, so
+    importance scores (and with them the top-k selection) are bit-identical
+    across implementations.
 """
 from __future__ import annotations
 
@@ -23,7 +25,7 @@ def normal(g: torch.Generator, shape) -> torch.Tensor:
 
 
 def grid(g: torch.Generator, shape) -> torch.Tensor:
-    return torch.randint(-64, 64, shape, generator=g).float() * (1.0 / 16.0)
+    return torch.randint(-32, 32, shape, generator=g).float() * (1.0 / 32.0)
 
 
 def make(kind: str, g: torch.Generator, shape) -> torch.Tensor:
