@@ -25,9 +25,7 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -39,7 +37,7 @@ for _p in (REPO, PKG_ROOT):
 import torch  # noqa: E402
 
 METRIC = "non-causal attn TFLOP/s & step tokens/s at LLaDA-8B shape, 1/2/4/8 B200, % roofline"
-LAYERS, HEADS, KV_HEADS, HEAD_DIM, HIDDEN = 32, 32, 32, 128, 4096
+LAYERS, HEADS, KV_HEADS, HEAD_DIM, HIDDEN = 32, 32, 32, 128, 4096  # LAYERS: --layers
 BATCH, GEN = 16, 128
 
 
@@ -89,64 +87,78 @@ def profile_traffic(name: str):
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Polls the GPU's SM clock, power and clock-event reasons (read-only NVML
+    queries) every 20 ms while the timed region runs; falls back to
+    ``nvidia-smi -lms 100`` when NVML is unavailable."""
 
-    def __init__(self, gpu_index: int):
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+
+    def __init__(self, gpu_index: int, period_s: float = 0.02):
         self.gpu_index = gpu_index
-        self.proc = None
-        self.path = None
+        self.period = period_s
+        self.samples = []
+        self.err = None
+        self._stop = None
+        self._thread = None
 
     def __enter__(self):
+        import threading
+
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu_index)],
-                stdout=self.fh, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - report, never fail the bench
+            self.err = f"nvml unavailable: {e}"
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            nv, h = self._nv, self._h
+            while not self._stop.is_set():
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, pw, rs))
+                except Exception as e:  # noqa: BLE001
+                    self.err = str(e)
+                    return
+                self._stop.wait(self.period)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.fh.close()
+                self._nv.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
 
     def summary(self):
-        if self.proc is None or self.path is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-
-        def num(x):
-            try:
-                return float(x)
-            except ValueError:
-                return None
-
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
-        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows),
-                "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"]}
+        nv = self._nv
+        reasons = set()
+        for _, _, rs in self.samples:
+            for name, const in self.REASONS:
+                if hasattr(nv, const) and rs & getattr(nv, const):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(self.samples), "power_w_max": max(s[1] for s in self.samples),
+                "source": "NVML, 20 ms period, during the timed region"}
 
 
 def physical_gpu_index(local_rank: int) -> int:
@@ -497,6 +509,58 @@ def run_ours(args, lens):
     return 0
 
 
+def run_kernels_case(args):
+    """Small profiling case: each native kernel launched 3 times on inputs
+    larger than L2 (one c2 layer for attention and the KV store, config-5
+    shapes for scoring/top-k, config-3 reuse shapes for cached attention)."""
+    from dllmserve_b200 import _native, ops
+
+    _native.lib()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    lens = workload_lengths()
+    N = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device=dev)
+    rnd = lambda *shape: torch.randn(*shape, device=dev, dtype=torch.bfloat16, generator=g)
+    q, k, v = rnd(N, HEADS, HEAD_DIM), rnd(N, KV_HEADS, HEAD_DIM), rnd(N, KV_HEADS, HEAD_DIM)
+    for _ in range(3):
+        ops.varlen_attention(q, k, v, cu, cu, max(lens))
+    pages = (N + 255) // 256 + 8
+    kc = torch.zeros(pages, 256, KV_HEADS, HEAD_DIM, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slot = torch.randperm(pages * 256, device=dev, generator=g)[:N].to(torch.int32)
+    for _ in range(3):
+        ops.store_kvcache(k, v, kc, vc, slot)
+    del q, k, v
+    # config 5: B=8, L=4096+512, block 32 at the start of the generation, r=0.25
+    B5, L5, blk = 8, 4608, 32
+    q5, k5, v5 = rnd(B5 * L5, HEADS, HEAD_DIM), rnd(B5 * L5, KV_HEADS, HEAD_DIM), rnd(B5 * L5, KV_HEADS, HEAD_DIM)
+    n_keep = min(max(1, int((L5 - blk) * 0.25)), L5 - blk)
+    desc = torch.tensor([[b * L5, L5, 4096, blk, n_keep, b * n_keep, 0, 3] for b in range(B5)],
+                        dtype=torch.int32, device=dev)
+    pages5 = (B5 * n_keep + 255) // 256 + 8
+    kc5 = torch.zeros(pages5, 256, KV_HEADS, HEAD_DIM, device=dev, dtype=torch.bfloat16)
+    vc5 = torch.zeros_like(kc5)
+    slots5 = torch.randperm(pages5 * 256, device=dev, generator=g)[:B5 * n_keep].to(torch.int32)
+    for _ in range(3):
+        ops.select_kv_store(q5, k5, v5, desc, L5 - blk, True, kc5, vc5, slots5)
+    del q5, k5, v5
+    # config 3 reuse state: B=8, 32 block queries, 304 cached + 32 fresh keys
+    B3, n3 = 8, 304
+    q3, k3, v3 = rnd(B3 * 32, HEADS, HEAD_DIM), rnd(B3 * 32, KV_HEADS, HEAD_DIM), rnd(B3 * 32, KV_HEADS, HEAD_DIM)
+    kc3, vc3 = rnd(B3 * n3, KV_HEADS, HEAD_DIM), rnd(B3 * n3, KV_HEADS, HEAD_DIM)
+    cq = torch.arange(0, B3 * 32 + 1, 32, dtype=torch.int32, device=dev)
+    cc = torch.arange(0, B3 * n3 + 1, n3, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        ops.varlen_attention(q3, k3, v3, cq, cq, 32, k_cached=kc3, v_cached=vc3, cu_seqlens_c=cc)
+    torch.cuda.synchronize()
+    if ops.read_device_status(dev) != 0:
+        raise RuntimeError("a kernel reported a device error")
+    print(json.dumps({"kernels_case": "ok", "launches": ops.LAUNCHES[0]}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -506,8 +570,15 @@ def main():
     ap.add_argument("--skip-extras", action="store_true",
                     help="only the primary timed loop (used for profiling runs)")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--kernels-case", action="store_true",
+                    help="run each native kernel 3x on a small case (for ncu captures)")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers per step (32 = the workload; fewer only for profiling runs)")
     args = ap.parse_args()
+    globals()["LAYERS"] = args.layers
     lens = workload_lengths()
+    if args.kernels_case:
+        return run_kernels_case(args)
     if args.impl == "reference":
         return run_reference_arm(args, lens)
     return run_ours(args, lens)

@@ -295,18 +295,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
         tmem_wait_ld();
-        if (t.valid < kTileN) {
+        const bool partial = t.valid < kTileN;
+        if (partial) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e)
               if (c * 32 + e >= t.valid) s[c][e] = __float_as_uint(-INFINITY);
         }
-        float mx = -INFINITY;
+        // row max: four independent 3-input max chains
+        float mq[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 4; ++c) {
+          float a = __uint_as_float(s[c][0]);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(s[c][e]));
+          for (int e = 1; e < 31; e += 2)
+            a = max3f(a, __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]));
+          mq[c] = fmaxf(a, __uint_as_float(s[c][31]));
+        }
+        const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
         const float mxs = mx * sl2;
         bool rescale = false;
         float alpha = 1.f;
@@ -326,19 +333,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float neg_m = -m;
-        float rs = 0.f;
+        float rsa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
-            rs += p0 + p1;
+            float x0, x1, p0, p1;
+            fma2(x0, x1, __uint_as_float(s[c][2 * e]), __uint_as_float(s[c][2 * e + 1]), sl2, sl2,
+                 neg_m, neg_m);
+            // 3 of every 8 pairs on the FMA pipe, the rest on MUFU; masked
+            // (partial) tiles stay on MUFU so masked columns are exactly 0.
+            if (!partial && (e & 7) < 3) {
+              exp2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2_approx(x0);
+              p1 = ex2_approx(x1);
+            }
+            add2(rsa[(e & 1) * 2], rsa[(e & 1) * 2 + 1], rsa[(e & 1) * 2], rsa[(e & 1) * 2 + 1], p0, p1);
             pk[e] = pack_bf16x2(p0, p1);
           }
           tmem_st16(tS + c * 16, pk);
         }
+        const float rs = (rsa[0] + rsa[1]) + (rsa[2] + rsa[3]);
         l += rs;
         if (rescale) {
 #pragma unroll

@@ -267,6 +267,57 @@ DLLM_DEVICE float ex2_approx(float x) {
   return y;
 }
 
+DLLM_DEVICE float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed two-lane fp32 FMA / add (Blackwell f32x2): d = a * b + c.
+DLLM_DEVICE void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                      float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+DLLM_DEVICE void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^x on the FMA pipe for two lanes (x <= ~126). Cody-Waite style range
+// reduction x = n + f, n = nearest integer (via the 1.5*2^23 rounding
+// constant), f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients
+// were fitted for this library (iteratively reweighted least squares on
+// Chebyshev nodes, max relative error 7.5e-5 - far below bf16's 2^-9);
+// 2^n is applied by adding n to the exponent field. Inputs below -125 are
+// clamped there (result ~2e-38 instead of 0), so callers keep masked (-inf)
+// columns on the MUFU path.
+constexpr float kExp2C0 = 0.9999280571937561f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.2426111400127411f;
+constexpr float kExp2C3 = 0.0551716573536396f;
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+DLLM_DEVICE void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  float t0, t1, n0, n1, f0, f1, p0, p1;
+  add2(t0, t1, x0, x1, kRoundMagic, kRoundMagic);
+  add2(n0, n1, t0, t1, -kRoundMagic, -kRoundMagic);
+  fma2(f0, f1, n0, n1, -1.f, -1.f, x0, x1);
+  fma2(p0, p1, kExp2C3, kExp2C3, f0, f1, kExp2C2, kExp2C2);
+  fma2(p0, p1, p0, p1, f0, f1, kExp2C1, kExp2C1);
+  fma2(p0, p1, p0, p1, f0, f1, kExp2C0, kExp2C0);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 DLLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
