@@ -24,7 +24,7 @@ SOURCES = ["attn_fwd.cu", "kvcache.cu", "select_kv.cu", "capi.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
-    "-Xcompiler", "-fPIC,-fvisibility=hidden",
+    "-Xcompiler", "-fPIC,-fvisibility=hidden", "-Xlinker", "--no-undefined",
     "--expt-relaxed-constexpr",
     "-shared",
 ]

@@ -5,12 +5,13 @@
 // including the cached-K/V ("reuse") sequences whose keys are the selected
 // cached rows followed by the block's fresh rows (attention.py:235-265).
 //
-// Work unit: one CTA = (sequence b, query head h, pair of 128-row query tiles).
-// Roles inside the CTA (10 warps):
+// Persistent kernel: one CTA per SM loops over work units = (sequence b,
+// query head h, pair of 128-row query tiles). Roles inside the CTA (11 warps):
 //   warps 0-3  softmax warpgroup 0  (query tile 0, TMEM lanes 0-127)
 //   warps 4-7  softmax warpgroup 1  (query tile 1)
-//   warp  8    TMA producer          (Q once, K/V ring of kStages)
-//   warp  9    MMA issuer            (also allocates / frees TMEM)
+//   warp  8    TMA producer: Q tiles and the K ring (kStagesK deep)
+//   warp  9    MMA issuer (also allocates / frees TMEM)
+//   warp  10   TMA producer: the V ring (kStagesV deep)
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P_i (bf16) is written over the first 64 columns of S_i. The MMA issue
 // order per KV tile j is  PV_i(j) then QK_i(j+1) for each tile i, so the next
@@ -31,30 +32,40 @@ namespace {
 constexpr int kD = 128;          // head dim (only 128 is instantiated)
 constexpr int kTileM = 128;      // query rows per tile
 constexpr int kTileN = 128;      // kv rows per tile
-constexpr int kStages = 2;       // K and V ring depth
-constexpr int kThreads = 320;
+constexpr int kStagesK = 3;      // K ring depth (K runs one tile ahead of V)
+constexpr int kStagesV = 2;      // V ring depth
+constexpr int kThreads = 352;
+
+// Softmax code-shape switches (tuning; defaults are the measured best).
+#ifndef DLLM_SM_POLY
+#define DLLM_SM_POLY 0
+#endif
+constexpr int kSmPoly = DLLM_SM_POLY;         // pairs of 8 evaluated on the FMA pipe
 constexpr uint32_t kTileBytes = kTileM * kD * 2;  // 32 KB (bf16)
 constexpr uint32_t kChunkBytes = 128 * 128;       // 128 rows x 128 B (64 bf16)
 
 // Shared-memory map (offsets from a 1024-aligned base).
 constexpr uint32_t kOffQ = 0;                                   // 2 tiles
-constexpr uint32_t kOffK = kOffQ + 2 * kTileBytes;              // kStages tiles
-constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;        // kStages tiles
-constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;      // barriers
-constexpr uint32_t kNumBars = 1 + 4 * kStages + 2 + 2 + 2 + 1;
+constexpr uint32_t kOffK = kOffQ + 2 * kTileBytes;              // kStagesK tiles
+constexpr uint32_t kOffV = kOffK + kStagesK * kTileBytes;       // kStagesV tiles
+constexpr uint32_t kOffBar = kOffV + kStagesV * kTileBytes;     // barriers
+constexpr uint32_t kNumBars = 2 + 2 * kStagesK + 2 * kStagesV + 2 + 2 + 2 + 1;
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;          // + alignment slack
 
 // barrier indices
 constexpr int BAR_Q = 0;
-constexpr int BAR_KFULL = 1;
-constexpr int BAR_KEMPTY = BAR_KFULL + kStages;
-constexpr int BAR_VFULL = BAR_KEMPTY + kStages;
-constexpr int BAR_VEMPTY = BAR_VFULL + kStages;
-constexpr int BAR_SFULL = BAR_VEMPTY + kStages;  // 2
+constexpr int BAR_QEMPTY = 1;
+constexpr int BAR_KFULL = 2;
+constexpr int BAR_KEMPTY = BAR_KFULL + kStagesK;
+constexpr int BAR_VFULL = BAR_KEMPTY + kStagesK;
+constexpr int BAR_VEMPTY = BAR_VFULL + kStagesV;
+constexpr int BAR_SFULL = BAR_VEMPTY + kStagesV;  // 2
 constexpr int BAR_PFULL = BAR_SFULL + 2;         // 2
 constexpr int BAR_OFULL = BAR_PFULL + 2;         // 2
 constexpr int BAR_DRAIN = BAR_OFULL + 2;         // 1
+
+DLLM_DEVICE int row_in_tile_of(int tid) { return tid & 127; }
 
 struct KvTile {
   int seg;    // 0 = cached, 1 = fresh
@@ -80,8 +91,114 @@ DLLM_DEVICE KvTile kv_tile(int t, int nc, int c0, int nk, int k0) {
   return r;
 }
 
+#ifdef DLLM_TRACE
+// Debug-only event trace (never built into the shipped library): for every
+// 256th CTA (up to 16) each warp records (clock64, code) pairs into its own
+// slice after the status word; per-warp counters live in shared memory.
+__shared__ unsigned g_trace_cnt[16];
+DLLM_DEVICE void trace_rec(int32_t* err, int ev, int j, int tile) {
+  const unsigned cid = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (err == nullptr || (cid & 255u) != 0 || (cid >> 8) >= 16) return;
+  const int w = threadIdx.x >> 5;
+  const unsigned k = atomicAdd(&g_trace_cnt[w], 1u);
+  if (k >= 1024) return;
+  unsigned long long* region =
+      reinterpret_cast<unsigned long long*>(err + 16) + ((cid >> 8) * 16 + w) * 2048;
+  long long clk;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(clk));
+  region[2 * k] = (unsigned long long)clk;
+  region[2 * k + 1] = (unsigned long long)(ev | (j << 8) | (tile << 20) | (w << 24));
+}
+#define TRACE(ev, j, tile) trace_rec(args.err, ev, j, tile)
+__device__ int32_t* trace_err;
+#else
+#define TRACE(ev, j, tile) \
+  do {                     \
+  } while (0)
+#endif
+
+
+// P = 2^(S*scale_log2 - m) for one row of a 128-column tile, packed to bf16
+// pairs and stored to TMEM over the first 64 columns of the S tile; returns
+// the row sum of P (fp32). kPoly of every 8 column pairs use the FMA-pipe
+// exp2, the rest MUFU ex2 (the split is fixed at compile time so no path is
+// evaluated twice).
+template <int kPoly>
+DLLM_DEVICE float exp_store_tile(const uint32_t (&s)[4][32], float sl2, float m, uint32_t tS) {
+  const f32x2_t sl2x2 = pk2(sl2, sl2);
+  const f32x2_t negm2 = pk2(-m, -m);
+  f32x2_t rsa[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const f32x2_t x = ffma2(pk2u(s[c][2 * e], s[c][2 * e + 1]), sl2x2, negm2);
+      f32x2_t p;
+      if ((e & 7) < kPoly) {
+        p = exp2_poly2(x);
+      } else {
+        float x0, x1;
+        upk2(x, x0, x1);
+        p = pk2(ex2_approx(x0), ex2_approx(x1));
+      }
+      rsa[e & 1] = fadd2(rsa[e & 1], p);
+      float p0, p1;
+      upk2(p, p0, p1);
+      pk[e] = pack_bf16x2(p0, p1);
+    }
+    tmem_st16(tS + c * 16, pk);
+#ifdef DLLM_TRACE
+    if ((threadIdx.x & 127) == 0) trace_rec(trace_err, 17 + c, 0, 0);
+#endif
+  }
+  float r0, r1, r2, r3;
+  upk2(rsa[0], r0, r1);
+  upk2(rsa[1], r2, r3);
+  return (r0 + r1) + (r2 + r3);
+}
+
 }  // namespace
 
+// One work unit: (sequence b, query head hq, pair p of 128-row query tiles).
+struct Unit {
+  bool valid;
+  int hq, hkv;
+  int q_begin, Lq, q0, ntiles;
+  int k_begin, nk, c_begin, nc, nkv;
+};
+
+// Units are numbered ((b * Hq) + hq) * qpairs + p, so consecutive units share
+// a sequence and head (their K/V stay hot in L2 while several CTAs read them).
+DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
+  Unit r;
+  const int per_b = a.Hq * a.qpairs;
+  const int b = u / per_b;
+  const int rem = u - b * per_b;
+  r.hq = rem / a.qpairs;
+  const int p = rem - r.hq * a.qpairs;
+  r.hkv = r.hq / a.group;
+  r.q_begin = a.cu_q[b];
+  r.Lq = a.cu_q[b + 1] - r.q_begin;
+  r.q0 = p * 2 * kTileM;
+  r.valid = r.q0 < r.Lq;
+  r.ntiles = (r.Lq - r.q0 > kTileM) ? 2 : 1;
+  r.k_begin = a.cu_k[b];
+  r.nk = a.cu_k[b + 1] - r.k_begin;
+  r.c_begin = 0;
+  r.nc = 0;
+  if (a.cu_c != nullptr) {
+    r.c_begin = a.cu_c[b];
+    r.nc = a.cu_c[b + 1] - r.c_begin;
+  }
+  r.nkv = (r.nc + kTileN - 1) / kTileN + (r.nk + kTileN - 1) / kTileN;
+  return r;
+}
+
+// Persistent kernel: CTA c processes units c, c + gridDim.x, ... Barrier
+// phases run on across units (ring counters below), so the producer loads the
+// next unit's Q/K/V and the MMA warp starts its QK while the softmax warps
+// still write the previous unit's output.
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
@@ -93,42 +210,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  const int b = blockIdx.z;
-  const int hq = blockIdx.y;
-  const int hkv = hq / args.group;
-
-  const int q_begin = args.cu_q[b];
-  const int Lq = args.cu_q[b + 1] - q_begin;
-  const int q0 = blockIdx.x * (2 * kTileM);
-  if (q0 >= Lq) return;  // uniform for the CTA
-  const int ntiles = (Lq - q0 > kTileM) ? 2 : 1;
-
-  const int k_begin = args.cu_k[b];
-  const int nk = args.cu_k[b + 1] - k_begin;
-  int c_begin = 0, nc = 0;
-  if (args.cu_c != nullptr) {
-    c_begin = args.cu_c[b];
-    nc = args.cu_c[b + 1] - c_begin;
-  }
-  const int nkv = (nc + kTileN - 1) / kTileN + (nk + kTileN - 1) / kTileN;
+  const int total_units = args.total_units;
 
   const uint32_t bar0 = base + kOffBar;
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc + 16);
 
+#ifdef DLLM_TRACE
+  if (threadIdx.x < 16) g_trace_cnt[threadIdx.x] = 0;
+  if (threadIdx.x == 0) trace_err = args.err;
+#endif
   if (threadIdx.x == 0) {
     mbar_init(bar(BAR_Q), 1);
-    for (int s = 0; s < kStages; ++s) {
+    mbar_init(bar(BAR_QEMPTY), 1);
+    for (int s = 0; s < kStagesK; ++s) {
       mbar_init(bar(BAR_KFULL + s), 1);
       mbar_init(bar(BAR_KEMPTY + s), 1);
+    }
+    for (int s = 0; s < kStagesV; ++s) {
       mbar_init(bar(BAR_VFULL + s), 1);
       mbar_init(bar(BAR_VEMPTY + s), 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(BAR_SFULL + i), 1);
-      mbar_init(bar(BAR_PFULL + i), 128);
+      mbar_init(bar(BAR_PFULL + i), 4);  // one arrival per softmax warp
       mbar_init(bar(BAR_OFULL + i), 1);
     }
     mbar_init(bar(BAR_DRAIN), 1);
@@ -143,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
-    if (nc > 0) {
+    if (args.cu_c != nullptr) {
       tma_prefetch_desc(&tmKc);
       tma_prefetch_desc(&tmVc);
     }
@@ -152,121 +258,163 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 9 * 32) TRACE(1, 0, 0);
 
-  if (warp == 8) {
+  if (warp == 8 || warp == 10) {
     // ------------------------------------------------------------------ TMA
+    // warp 8: Q and K tiles; warp 10: V tiles (independent rings, so a wait
+    // for a free V stage never holds back a K load and vice versa).
     if (lane == 0) {
+      const bool kq = warp == 8;
       const uint64_t pol_q = policy_evict_first();
       const uint64_t pol_kv = policy_evict_last();
-      // Q: both tiles, two 64-column chunks each.
-      mbar_arrive_expect_tx(bar(BAR_Q), ntiles * kTileBytes);
-      for (int i = 0; i < ntiles; ++i) {
-        const uint32_t dst = base + kOffQ + i * kTileBytes;
-        const int row = q_begin + q0 + i * kTileM;
-        tma_load_3d(dst, &tmQ, bar(BAR_Q), 0, hq, row, pol_q);
-        tma_load_3d(dst + kChunkBytes, &tmQ, bar(BAR_Q), 64, hq, row, pol_q);
-      }
-      int issued = 0;
+      const int nst = kq ? kStagesK : kStagesV;
+      const int bfull = kq ? BAR_KFULL : BAR_VFULL;
+      const int bempty = kq ? BAR_KEMPTY : BAR_VEMPTY;
+      const uint32_t ring = base + (kq ? kOffK : kOffV);
+      uint32_t q_it = 0;     // units whose Q was loaded (warp 8)
+      uint32_t done = 0;     // tiles issued into this ring
       bool ok = true;
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j % kStages;
-        const uint32_t use = (uint32_t)(j / kStages);
-        const KvTile t = kv_tile(j, nc, c_begin, nk, k_begin);
-        const CUtensorMap* mk = t.seg == 0 ? &tmKc : &tmK;
-        const CUtensorMap* mv = t.seg == 0 ? &tmVc : &tmV;
-        if (j >= kStages) ok = mbar_wait(bar(BAR_KEMPTY + st), (use - 1) & 1, abort_flag);
-        if (!ok) break;
-        uint32_t dk = base + kOffK + st * kTileBytes;
-        mbar_arrive_expect_tx(bar(BAR_KFULL + st), kTileBytes);
-        tma_load_3d(dk, mk, bar(BAR_KFULL + st), 0, hkv, t.row0, pol_kv);
-        tma_load_3d(dk + kChunkBytes, mk, bar(BAR_KFULL + st), 64, hkv, t.row0, pol_kv);
-        if (j >= kStages) ok = mbar_wait(bar(BAR_VEMPTY + st), (use - 1) & 1, abort_flag);
-        if (!ok) {
-          issued = j + 1;  // K of tile j is in flight
-          break;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        const Unit t = decode_unit(u, args);
+        if (!t.valid) continue;
+        if (kq) {
+          if (q_it > 0) ok = mbar_wait(bar(BAR_QEMPTY), (q_it - 1) & 1, abort_flag);
+          if (!ok) break;
+          mbar_arrive_expect_tx(bar(BAR_Q), t.ntiles * kTileBytes);
+          for (int i = 0; i < t.ntiles; ++i) {
+            const uint32_t dst = base + kOffQ + i * kTileBytes;
+            const int row = t.q_begin + t.q0 + i * kTileM;
+            tma_load_3d(dst, &tmQ, bar(BAR_Q), 0, t.hq, row, pol_q);
+            tma_load_3d(dst + kChunkBytes, &tmQ, bar(BAR_Q), 64, t.hq, row, pol_q);
+          }
+          ++q_it;
         }
-        uint32_t dv = base + kOffV + st * kTileBytes;
-        mbar_arrive_expect_tx(bar(BAR_VFULL + st), kTileBytes);
-        tma_load_3d(dv, mv, bar(BAR_VFULL + st), 0, hkv, t.row0, pol_kv);
-        tma_load_3d(dv + kChunkBytes, mv, bar(BAR_VFULL + st), 64, hkv, t.row0, pol_kv);
-        issued = j + 1;
+        for (int j = 0; j < t.nkv; ++j) {
+          const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+          const CUtensorMap* mp = kq ? (kt.seg == 0 ? &tmKc : &tmK) : (kt.seg == 0 ? &tmVc : &tmV);
+          const int st = done % nst;
+          if (done >= (uint32_t)nst) ok = mbar_wait(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
+          if (!ok) break;
+          const uint32_t dk = ring + st * kTileBytes;
+          mbar_arrive_expect_tx(bar(bfull + st), kTileBytes);
+          tma_load_3d(dk, mp, bar(bfull + st), 0, t.hkv, kt.row0, pol_kv);
+          tma_load_3d(dk + kChunkBytes, mp, bar(bfull + st), 64, t.hkv, kt.row0, pol_kv);
+          ++done;
+          TRACE(kq ? 2 : 3, j, 0);
+        }
       }
       if (*abort_flag) {
         // Drain: wait (bounded) for the loads that may still be in flight.
-        mbar_wait_drain(bar(BAR_Q), 0, 100000000ull);
-        for (int j = max(0, issued - kStages); j < issued; ++j) {
-          const int st = j % kStages;
-          const uint32_t use = (uint32_t)(j / kStages);
-          mbar_wait_drain(bar(BAR_KFULL + st), use & 1, 100000000ull);
-          mbar_wait_drain(bar(BAR_VFULL + st), use & 1, 100000000ull);
-        }
+        if (kq && q_it > 0) mbar_wait_drain(bar(BAR_Q), (q_it - 1) & 1, 100000000ull);
+        for (uint32_t n = (done > (uint32_t)nst ? done - nst : 0); n < done; ++n)
+          mbar_wait_drain(bar(bfull + n % nst), (n / nst) & 1, 100000000ull);
       }
     }
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
+      // Shared-memory descriptors are precomputed per buffer; a K-step adds a
+      // constant to the 14-bit start-address field (all offsets stay inside
+      // the 256 KB shared window, so the field never carries).
       const uint32_t idesc_pv = make_idesc_bf16(128, 128, true);
+      const uint32_t idesc_qk_full = make_idesc_bf16(128, 128, false);
+      // Buffers of one kind are kTileBytes apart: stage n adds n * (kTileBytes >> 4).
+      const uint64_t dq0 = make_sw128_desc(base + kOffQ, 16, 1024);
+      const uint64_t dk0 = make_sw128_desc(base + kOffK, 16, 1024);
+      const uint64_t dv0 = make_sw128_desc(base + kOffV, kChunkBytes, 1024);
+      constexpr uint64_t kStageStep = kTileBytes >> 4;
       auto qk = [&](int i, int st, int n_rows) {
-        const uint32_t qa = base + kOffQ + i * kTileBytes;
-        const uint32_t ka = base + kOffK + st * kTileBytes;
-        const int n = (n_rows + 15) & ~15;
-        const uint32_t idesc = make_idesc_bf16(128, n, false);
+        const uint32_t idesc =
+            n_rows == kTileN ? idesc_qk_full : make_idesc_bf16(128, (n_rows + 15) & ~15, false);
+        const uint64_t a = dq0 + (uint64_t)i * kStageStep, b = dk0 + (uint64_t)st * kStageStep;
+        const uint32_t d = tmem + i * 128;
 #pragma unroll
         for (int s = 0; s < kD / 16; ++s) {
-          const uint32_t off = (s >> 2) * kChunkBytes + (s & 3) * 32;
-          umma_ss(tmem + i * 128, make_sw128_desc(qa + off, 16, 1024),
-                  make_sw128_desc(ka + off, 16, 1024), idesc, s > 0 ? 1u : 0u);
+          const uint64_t off = (uint64_t)(((s >> 2) * kChunkBytes + (s & 3) * 32) >> 4);
+          umma_ss(d, a + off, b + off, idesc, s > 0 ? 1u : 0u);
         }
       };
       auto pv = [&](int i, int st, int n_rows, bool acc) {
-        const uint32_t va = base + kOffV + st * kTileBytes;
-        const int ksteps = (n_rows + 15) >> 4;
-        for (int s = 0; s < ksteps; ++s) {
-          umma_ts(tmem + 256 + i * 128, tmem + i * 128 + s * 8,
-                  make_sw128_desc(va + s * 2048, kChunkBytes, 1024), idesc_pv,
-                  (acc || s > 0) ? 1u : 0u);
+        const uint64_t b = dv0 + (uint64_t)st * kStageStep;
+        const uint32_t d = tmem + 256 + i * 128;
+        const uint32_t a = tmem + i * 128;
+        if (n_rows == kTileN) {
+#pragma unroll
+          for (int s = 0; s < 8; ++s)
+            umma_ts(d, a + s * 8, b + (uint64_t)(s * (2048 >> 4)), idesc_pv, (acc || s > 0) ? 1u : 0u);
+        } else {
+          const int ksteps = (n_rows + 15) >> 4;
+          for (int s = 0; s < ksteps; ++s)
+            umma_ts(d, a + s * 8, b + (uint64_t)(s * (2048 >> 4)), idesc_pv, (acc || s > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(bar(BAR_Q), 0, abort_flag);
-      if (ok && nkv > 0) ok = mbar_wait(bar(BAR_KFULL + 0), 0, abort_flag);
-      if (ok && nkv > 0) {
-        tc_fence_after();
-        const KvTile t0 = kv_tile(0, nc, c_begin, nk, k_begin);
-        for (int i = 0; i < ntiles; ++i) {
-          qk(i, 0, t0.valid);
-          umma_commit(bar(BAR_SFULL + i));
-        }
-        umma_commit(bar(BAR_KEMPTY + 0));
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int vst = j % kStages;
-        const KvTile t = kv_tile(j, nc, c_begin, nk, k_begin);
-        ok = mbar_wait(bar(BAR_VFULL + vst), (uint32_t)(j / kStages) & 1, abort_flag);
+      uint32_t q_it = 0, kv_it = 0;
+      uint32_t p_it[2] = {0, 0};
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        const Unit t = decode_unit(u, args);
+        if (!t.valid) continue;
+        ok = mbar_wait(bar(BAR_Q), q_it & 1, abort_flag);
         if (!ok) break;
-        const bool more = j + 1 < nkv;
-        const int kst = (j + 1) % kStages;
-        KvTile tn = t;
-        if (more) {
-          tn = kv_tile(j + 1, nc, c_begin, nk, k_begin);
-          ok = mbar_wait(bar(BAR_KFULL + kst), (uint32_t)((j + 1) / kStages) & 1, abort_flag);
-          if (!ok) break;
+        ++q_it;
+        if (t.nkv == 0) {
+          umma_commit(bar(BAR_QEMPTY));
+          continue;
         }
-        for (int i = 0; i < ntiles; ++i) {
-          ok = mbar_wait(bar(BAR_PFULL + i), (uint32_t)j & 1, abort_flag);
+        {
+          const int st0 = kv_it % kStagesK;
+          ok = mbar_wait(bar(BAR_KFULL + st0), (kv_it / kStagesK) & 1, abort_flag);
           if (!ok) break;
+          TRACE(4, 0, 0);
           tc_fence_after();
-          pv(i, vst, t.valid, j > 0);
-          if (more) {
-            qk(i, kst, tn.valid);
+          const KvTile t0 = kv_tile(0, t.nc, t.c_begin, t.nk, t.k_begin);
+          for (int i = 0; i < t.ntiles; ++i) {
+            qk(i, st0, t0.valid);
             umma_commit(bar(BAR_SFULL + i));
-          } else {
-            umma_commit(bar(BAR_OFULL + i));
           }
+          umma_commit(bar(BAR_KEMPTY + st0));
+          if (t.nkv == 1) umma_commit(bar(BAR_QEMPTY));
         }
-        if (!ok) break;
-        umma_commit(bar(BAR_VEMPTY + vst));
-        if (more) umma_commit(bar(BAR_KEMPTY + kst));
+        for (int j = 0; j < t.nkv && ok; ++j) {
+          const uint32_t kvj = kv_it + j;
+          const int vst = kvj % kStagesV;
+          const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+          ok = mbar_wait(bar(BAR_VFULL + vst), (kvj / kStagesV) & 1, abort_flag);
+          if (!ok) break;
+          TRACE(5, j, 0);
+          const bool more = j + 1 < t.nkv;
+          const int kst = (kvj + 1) % kStagesK;
+          const KvTile tn = more ? kv_tile(j + 1, t.nc, t.c_begin, t.nk, t.k_begin) : kt;
+          bool k_ready = !more;
+          for (int i = 0; i < t.ntiles; ++i) {
+            ok = mbar_wait(bar(BAR_PFULL + i), p_it[i] & 1, abort_flag);
+            if (!ok) break;
+            ++p_it[i];
+            TRACE(6, j, i);
+            tc_fence_after();
+            pv(i, vst, kt.valid, j > 0);
+            if (more) {
+              if (!k_ready) {
+                ok = mbar_wait(bar(BAR_KFULL + kst), ((kvj + 1) / kStagesK) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                k_ready = true;
+              }
+              qk(i, kst, tn.valid);
+              umma_commit(bar(BAR_SFULL + i));
+            } else {
+              umma_commit(bar(BAR_OFULL + i));
+            }
+            TRACE(7, j, i);
+          }
+          if (!ok) break;
+          umma_commit(bar(BAR_VEMPTY + vst));
+          if (more) umma_commit(bar(BAR_KEMPTY + kst));
+          if (more && j + 2 == t.nkv) umma_commit(bar(BAR_QEMPTY));  // last QK issued
+        }
+        kv_it += t.nkv;
       }
       // Make sure every issued MMA has finished before TMEM is released.
       umma_commit(bar(BAR_DRAIN));
@@ -278,30 +426,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wg = warp >> 2;           // 0 or 1: query tile
     const int wq = warp & 3;            // warp within the warpgroup
     const int row_in_tile = threadIdx.x & 127;
-    if (wg < ntiles) {
-      const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-      const uint32_t tS = tmem + lane_base + wg * 128;
-      const uint32_t tO = tmem + lane_base + 256 + wg * 128;
-      const float sl2 = args.scale_log2;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_base + wg * 128;
+    const uint32_t tO = tmem + lane_base + 256 + wg * 128;
+    const float sl2 = args.scale_log2;
+    uint32_t s_it = 0, o_it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      const Unit t = decode_unit(u, args);
+      if (!t.valid || wg >= t.ntiles) continue;
       float m = -INFINITY;
       float l = 0.f;
-      bool ok = true;
-      for (int j = 0; j < nkv; ++j) {
-        const KvTile t = kv_tile(j, nc, c_begin, nk, k_begin);
-        ok = mbar_wait(bar(BAR_SFULL + wg), (uint32_t)j & 1, abort_flag);
+      for (int j = 0; j < t.nkv; ++j) {
+        const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+        ok = mbar_wait(bar(BAR_SFULL + wg), s_it & 1, abort_flag);
         if (!ok) break;
+        ++s_it;
+        if (row_in_tile == 0) TRACE(10, j, wg);
         tc_fence_after();
         uint32_t s[4][32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
         tmem_wait_ld();
-        const bool partial = t.valid < kTileN;
+        if (row_in_tile == 0) TRACE(11, j, wg);
+        const bool partial = kt.valid < kTileN;
         if (partial) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              if (c * 32 + e >= t.valid) s[c][e] = __float_as_uint(-INFINITY);
+              if (c * 32 + e >= kt.valid) s[c][e] = __float_as_uint(-INFINITY);
         }
         // row max: four independent 3-input max chains
         float mq[4];
@@ -313,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             a = max3f(a, __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]));
           mq[c] = fmaxf(a, __uint_as_float(s[c][31]));
         }
-        const float mx = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3]));
-        const float mxs = mx * sl2;
+        const float mxs = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3])) * sl2;
+        if (row_in_tile == 0) TRACE(16, j, wg);
         bool rescale = false;
         float alpha = 1.f;
         if (j == 0) {
@@ -332,30 +486,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             rescale = true;
           }
         }
-        const float neg_m = -m;
-        float rsa[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float x0, x1, p0, p1;
-            fma2(x0, x1, __uint_as_float(s[c][2 * e]), __uint_as_float(s[c][2 * e + 1]), sl2, sl2,
-                 neg_m, neg_m);
-            // 3 of every 8 pairs on the FMA pipe, the rest on MUFU; masked
-            // (partial) tiles stay on MUFU so masked columns are exactly 0.
-            if (!partial && (e & 7) < 3) {
-              exp2_poly2(x0, x1, p0, p1);
-            } else {
-              p0 = ex2_approx(x0);
-              p1 = ex2_approx(x1);
-            }
-            add2(rsa[(e & 1) * 2], rsa[(e & 1) * 2 + 1], rsa[(e & 1) * 2], rsa[(e & 1) * 2 + 1], p0, p1);
-            pk[e] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16(tS + c * 16, pk);
+        float rs;
+        if (partial) {
+          rs = exp_store_tile<0>(s, sl2, m, tS);  // masked columns: MUFU only (exact 0)
+        } else {
+          rs = exp_store_tile<kSmPoly>(s, sl2, m, tS);
         }
-        const float rs = (rsa[0] + rsa[1]) + (rsa[2] + rsa[3]);
+        if (row_in_tile == 0) TRACE(12, j, wg);
         l += rs;
         if (rescale) {
 #pragma unroll
@@ -370,15 +507,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(BAR_PFULL + wg));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(BAR_PFULL + wg));
+        if (row_in_tile == 0) TRACE(13, j, wg);
       }
+      if (!ok) break;
       // Epilogue: O / l -> bf16 -> global.
-      const int row = q0 + wg * kTileM + row_in_tile;
-      const bool row_ok = row < Lq;
-      __nv_bfloat16* orow = args.o + (int64_t)(q_begin + row) * args.o_tok_stride +
-                            (int64_t)hq * args.o_head_stride;
-      if (ok && nkv > 0) ok = mbar_wait(bar(BAR_OFULL + wg), 0, abort_flag);
-      if (ok && nkv > 0) {
+      const int row = t.q0 + wg * kTileM + row_in_tile;
+      const bool row_ok = row < t.Lq;
+      __nv_bfloat16* orow = args.o + (int64_t)(t.q_begin + row) * args.o_tok_stride +
+                            (int64_t)t.hq * args.o_head_stride;
+      if (t.nkv > 0) {
+        ok = mbar_wait(bar(BAR_OFULL + wg), o_it & 1, abort_flag);
+        if (!ok) break;
+        ++o_it;
+        if (row_in_tile == 0) TRACE(14, 0, wg);
         tc_fence_after();
         const float inv_l = 1.f / l;
 #pragma unroll
@@ -399,7 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-      } else if (ok && nkv == 0 && row_ok) {
+        // O_i is read out; the next unit's first PV may overwrite it once this
+        // warpgroup arrives on its first P barrier (program order + fence).
+        tc_fence_before();
+      } else if (row_ok) {
         // No keys at all: the output row is zero.
         uint4* dst = reinterpret_cast<uint4*>(orow);
         for (int v = 0; v < kD / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
@@ -407,6 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (warp < 8 && row_in_tile_of(threadIdx.x) == 0) TRACE(15, 0, warp >> 2);
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {
@@ -417,10 +564,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 uint32_t attn_fwd_smem_bytes() { return kSmemBytes; }
+int attn_fwd_kv_rows_per_tile() { return kTileN; }
 
 cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                             const CUtensorMap& tmKc, const CUtensorMap& tmVc,
-                            const AttnKernelArgs& args, int max_q, cudaStream_t stream) {
+                            const AttnKernelArgs& args, int max_q, int num_sms,
+                            cudaStream_t stream) {
   // The smem opt-in is per device; remember it for up to 64 devices.
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -432,9 +581,14 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, cons
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  dim3 grid((max_q + 2 * kTileM - 1) / (2 * kTileM), args.Hq, args.B);
-  if (grid.x == 0 || args.B == 0) return cudaSuccess;
-  attn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmKc, tmVc, args);
+  AttnKernelArgs a = args;
+  a.qpairs = (max_q + 2 * kTileM - 1) / (2 * kTileM);
+  const long long units = (long long)a.B * a.Hq * a.qpairs;
+  if (units == 0) return cudaSuccess;
+  if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
+  a.total_units = (int)units;
+  const int grid = (int)(units < num_sms ? units : num_sms);
+  attn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmKc, tmVc, a);
   return cudaGetLastError();
 }
 

@@ -22,12 +22,16 @@ struct AttnKernelArgs {
   int group;               // Hq / Hkv
   float scale_log2;        // softmax_scale * log2(e)
   int32_t* err;            // optional device status word
+  int qpairs;              // 256-row query tile pairs per (sequence, head); set by the launcher
+  int total_units;         // B * Hq * qpairs; set by the launcher
 };
 
 uint32_t attn_fwd_smem_bytes();
+int attn_fwd_kv_rows_per_tile();  // rows of a key/value TMA box
 
 cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                             const CUtensorMap& tmKc, const CUtensorMap& tmVc,
-                            const AttnKernelArgs& args, int max_q, cudaStream_t stream);
+                            const AttnKernelArgs& args, int max_q, int num_sms,
+                            cudaStream_t stream);
 
 }  // namespace dllm

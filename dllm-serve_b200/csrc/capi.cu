@@ -64,14 +64,16 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 3-D map over [rows, heads, 128] bf16: dims (d, head, row), box (64, 1, 128),
-// 128-byte swizzle (matches the UMMA SW128 K-major / MN-major smem layout).
-int encode_rows_map(CUtensorMap* m, const void* ptr, int64_t rows, int heads, int64_t tok_stride) {
+// 3-D map over [rows, heads, 128] bf16: dims (d, head, row), box (64, 1,
+// box_rows), 128-byte swizzle (matches the UMMA SW128 K-major / MN-major smem
+// layout). Queries use 128-row boxes, keys/values 64-row boxes.
+int encode_rows_map(CUtensorMap* m, const void* ptr, int64_t rows, int heads, int64_t tok_stride,
+                    int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return fail(DLLM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)(rows > 0 ? rows : 1)};
   cuuint64_t strides[2] = {128 * 2, (cuuint64_t)tok_stride * 2};
-  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -120,12 +122,13 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
     if ((rc = check_rows("v_cached", vc, vc_tok_stride, Hkv, total_c)) != DLLM_OK) return rc;
   }
   CUtensorMap tq, tk, tv, tkc, tvc;
-  if ((rc = encode_rows_map(&tq, q, total_q, Hq, q_tok_stride)) != DLLM_OK) return rc;
-  if ((rc = encode_rows_map(&tk, k, total_k, Hkv, k_tok_stride)) != DLLM_OK) return rc;
-  if ((rc = encode_rows_map(&tv, v, total_k, Hkv, v_tok_stride)) != DLLM_OK) return rc;
+  const int kv_rows = dllm::attn_fwd_kv_rows_per_tile();
+  if ((rc = encode_rows_map(&tq, q, total_q, Hq, q_tok_stride, 128)) != DLLM_OK) return rc;
+  if ((rc = encode_rows_map(&tk, k, total_k, Hkv, k_tok_stride, kv_rows)) != DLLM_OK) return rc;
+  if ((rc = encode_rows_map(&tv, v, total_k, Hkv, v_tok_stride, kv_rows)) != DLLM_OK) return rc;
   if (cu_c != nullptr && total_c > 0) {
-    if ((rc = encode_rows_map(&tkc, kc, total_c, Hkv, kc_tok_stride)) != DLLM_OK) return rc;
-    if ((rc = encode_rows_map(&tvc, vc, total_c, Hkv, vc_tok_stride)) != DLLM_OK) return rc;
+    if ((rc = encode_rows_map(&tkc, kc, total_c, Hkv, kc_tok_stride, kv_rows)) != DLLM_OK) return rc;
+    if ((rc = encode_rows_map(&tvc, vc, total_c, Hkv, vc_tok_stride, kv_rows)) != DLLM_OK) return rc;
   } else {
     tkc = tk;
     tvc = tv;
@@ -144,7 +147,9 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.group = Hq / Hkv;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
-  cudaError_t e = dllm::launch_attn_fwd(tq, tk, tv, tkc, tvc, a, max_q,
+  a.qpairs = 0;
+  a.total_units = 0;
+  cudaError_t e = dllm::launch_attn_fwd(tq, tk, tv, tkc, tvc, a, max_q, num_sms_of_current_device(),
                                         reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
   return DLLM_OK;

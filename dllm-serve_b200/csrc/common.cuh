@@ -75,21 +75,33 @@ DLLM_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // lasts microseconds; the limit only ends a wait that can never complete.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or ~hint ns pass, instead of spinning in software (a
+// spinning warp steals issue slots from the warps that do the work).
+DLLM_DEVICE bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Returns false (and
 // raises *abort) when the time limit passes or another role already aborted;
 // callers then stop their loop and drain.
 DLLM_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
+  const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        return false;
-      }
+    if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;  // <= 0.2 ms per sleep
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
     }
   }
 }
@@ -273,24 +285,46 @@ DLLM_DEVICE float max3f(float a, float b, float c) {
   return d;
 }
 
-// Packed two-lane fp32 FMA / add (Blackwell f32x2): d = a * b + c.
-DLLM_DEVICE void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
-                      float c1) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-DLLM_DEVICE void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+DLLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// 2^x on the FMA pipe for two lanes (x <= ~126). Cody-Waite style range
+// Packed two-lane fp32 arithmetic (Blackwell f32x2). A pair lives in one
+// 64-bit register (low half = first element) so chains of pair operations
+// need no repacking.
+typedef unsigned long long f32x2_t;
+
+DLLM_DEVICE f32x2_t pk2(float lo, float hi) {
+  f32x2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+DLLM_DEVICE f32x2_t pk2u(uint32_t lo, uint32_t hi) {
+  f32x2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+DLLM_DEVICE void upk2(f32x2_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+DLLM_DEVICE f32x2_t ffma2(f32x2_t a, f32x2_t b, f32x2_t c) {  // a * b + c
+  f32x2_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+DLLM_DEVICE f32x2_t fadd2(f32x2_t a, f32x2_t b) {
+  f32x2_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+DLLM_DEVICE f32x2_t fmul2(f32x2_t a, f32x2_t b) {
+  f32x2_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x on the FMA pipe for a pair (x <= ~126). Cody-Waite style range
 // reduction x = n + f, n = nearest integer (via the 1.5*2^23 rounding
 // constant), f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients
 // were fitted for this library (iteratively reweighted least squares on
@@ -304,23 +338,21 @@ constexpr float kExp2C2 = 0.2426111400127411f;
 constexpr float kExp2C3 = 0.0551716573536396f;
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
 
-DLLM_DEVICE void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-  x0 = fmaxf(x0, -125.f);
-  x1 = fmaxf(x1, -125.f);
-  float t0, t1, n0, n1, f0, f1, p0, p1;
-  add2(t0, t1, x0, x1, kRoundMagic, kRoundMagic);
-  add2(n0, n1, t0, t1, -kRoundMagic, -kRoundMagic);
-  fma2(f0, f1, n0, n1, -1.f, -1.f, x0, x1);
-  fma2(p0, p1, kExp2C3, kExp2C3, f0, f1, kExp2C2, kExp2C2);
-  fma2(p0, p1, p0, p1, f0, f1, kExp2C1, kExp2C1);
-  fma2(p0, p1, p0, p1, f0, f1, kExp2C0, kExp2C0);
-  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
-DLLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+DLLM_DEVICE f32x2_t exp2_poly2(f32x2_t x) {
+  float x0, x1;
+  upk2(x, x0, x1);
+  x = pk2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const f32x2_t t = fadd2(x, pk2(kRoundMagic, kRoundMagic));
+  const f32x2_t n = fadd2(t, pk2(-kRoundMagic, -kRoundMagic));
+  const f32x2_t f = ffma2(n, pk2(-1.f, -1.f), x);
+  f32x2_t p = ffma2(pk2(kExp2C3, kExp2C3), f, pk2(kExp2C2, kExp2C2));
+  p = ffma2(p, f, pk2(kExp2C1, kExp2C1));
+  p = ffma2(p, f, pk2(kExp2C0, kExp2C0));
+  float p0, p1, t0, t1;
+  upk2(p, p0, p1);
+  upk2(t, t0, t1);
+  return pk2(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
+             __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
 }
 
 }  // namespace dllm
