@@ -509,6 +509,221 @@ def run_ours(args, lens):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# sparse diffusion-block cycle (configs 3, 4, 5) through the public layer API
+# ---------------------------------------------------------------------------
+SPARSE_WORKLOADS = {
+    # name: (layers, Hq, Hkv, batch, prompt (lo, hi), gen, ratio, description)
+    "c3": (32, 32, 32, 8, (512, 512), 128, 0.5,
+           "c3: LLaDA-8B head_select r=0.5, B=8, 512+128 tokens"),
+    "c4": (28, 28, 4, 32, (128, 768), 256, 0.5,
+           "c4: Dream-7B GQA 28/4 head_select r=0.5, B=32, U[128,768]+256 tokens"),
+    "c5": (32, 32, 32, 8, (4096, 4096), 512, 0.25,
+           "c5: LLaDA-8B long context head_select r=0.25, B=8, 4096+512 tokens"),
+}
+
+
+def run_sparse_cycle(args):
+    """One diffusion block = 32 denoising steps with SparseConfig(delay_step=1,
+    block 32): state 0 (dense), state 1 (dense + select/store), 30 x state 2
+    (block queries over cached + fresh keys), timed against 32 dense steps.
+    Every layer is the public Attention module driven through set_context,
+    as the model runner drives it; q/k/v are synthetic per layer."""
+    import torch.distributed as dist
+
+    from dllmserve_b200 import _native, ops
+    from dllmserve_b200.layers.attention import Attention
+    from dllmserve_b200.sparse.state import PerRequestSparseState, SparseConfig, num_keep
+    from dllmserve_b200.tp import head_slice
+    from dllmserve_b200.utils.context import reset_context, set_context
+
+    layers, Hq_all, Hkv_all, B, (plo, phi), gen, ratio, desc = SPARSE_WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    _native.lib()
+    h0, h1, k0, k1 = head_slice(Hq_all, Hkv_all, rank, world)
+    Hq, Hkv = h1 - h0, k1 - k0
+    g = torch.Generator().manual_seed(40 + int(args.workload[1]))
+    prompts = torch.randint(plo, phi + 1, (B,), generator=g).tolist()
+    lens = [p + gen for p in prompts]
+    blk = 32
+    cfg = SparseConfig(enabled=True, default_block_len=blk, retention_ratio=ratio, pool_kernel=3,
+                       delay_step=1, head_select=True)
+
+    class Seq:
+        def __init__(self, prompt, L, sparse):
+            self.num_prompt_tokens = prompt
+            self.num_tokens = L
+            self.sparse_state = PerRequestSparseState(0, cfg, dev) if sparse else None
+
+    n_keeps = [num_keep(L - blk, ratio) for L in lens]
+    pages_per = [(n + 255) // 256 for n in n_keeps]
+    total_pages = sum(pages_per) + 4
+    slots, pg = [], 0
+    for n, npg in zip(n_keeps, pages_per):
+        lst = []
+        for j in range(npg):
+            lst.extend(range((pg + j) * 256, (pg + j) * 256 + min(256, n - j * 256)))
+        pg += npg
+        slots.append(torch.tensor(lst, dtype=torch.int32, device=dev))
+    N_full = sum(lens)
+    gd = torch.Generator(device=dev).manual_seed(1000 + rank)
+    mk = lambda h: torch.randn(N_full, h, HEAD_DIM, device=dev, dtype=torch.bfloat16, generator=gd)
+    qs = [mk(Hq) for _ in range(layers)]
+    ks = [mk(Hkv) for _ in range(layers)]
+    vs = [mk(Hkv) for _ in range(layers)]
+    attn = []
+    for _ in range(layers):
+        a = Attention(Hq, HEAD_DIM, HEAD_DIM ** -0.5, Hkv, causal=False)
+        a.k_cache = torch.zeros(total_pages, 256, Hkv, HEAD_DIM, device=dev, dtype=torch.bfloat16)
+        a.v_cache = torch.zeros_like(a.k_cache)
+        attn.append(a)
+
+    from dllmserve_b200.utils.context import Context, use_context
+
+    def rows_of(seqs):
+        return sum(s.num_tokens if (s.sparse_state is None or s.sparse_state.cache_state != 2)
+                   else s.sparse_state.compute_block_boundaries(s.num_prompt_tokens, s.num_tokens)[1]
+                   for s in seqs)
+
+    def make_ctx(seqs):
+        return Context(is_prefill=True, is_diffusion=True, seqs=seqs,
+                       slot_mapping=[(sl if s.sparse_state is not None and s.sparse_state.cache_state
+                                      else []) for s, sl in zip(seqs, slots)])
+
+    def step(seqs, ctx=None):
+        rows = rows_of(seqs)
+        use_context(ctx if ctx is not None else make_ctx(seqs))
+        for l in range(layers):
+            attn[l](qs[l][:rows].view(rows, -1), ks[l][:rows].view(rows, -1),
+                    vs[l][:rows].view(rows, -1))
+        reset_context()
+        return rows
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def timed(fn, reps):
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    dense_seqs = [Seq(p, L, False) for p, L in zip(prompts, lens)]
+    for _ in range(max(1, args.warmup)):
+        step(dense_seqs)
+    dense_ms = timed(lambda: step(dense_seqs), max(1, min(args.steps, 10)))
+
+    sparse_seqs = [Seq(p, L, True) for p, L in zip(prompts, lens)]
+
+    def rewind():
+        for s in sparse_seqs:  # restart at the same block so every cycle sees the same shapes
+            s.sparse_state.current_block_idx = 0
+            s.sparse_state.step_in_block = 0
+            s.sparse_state.cache_state = 0
+
+    def advance():
+        for s in sparse_seqs:
+            s.sparse_state.advance_step()
+
+    # eager: every step builds its context (metadata H2D) and launches from Python
+    per_state = {0: [], 1: [], 2: []}
+    cycles = max(1, min(args.steps // 32, 3))
+    for _ in range(blk):  # warm-up cycle, also fills the caches
+        step(sparse_seqs)
+        advance()
+    rewind()
+    cycle_ms = []
+    for _ in range(cycles):
+        tot = 0.0
+        for _ in range(blk):
+            st = sparse_seqs[0].sparse_state.cache_state
+            ms = timed(lambda: step(sparse_seqs), 1)
+            per_state[st].append(ms)
+            tot += ms
+            advance()
+        rewind()
+        cycle_ms.append(tot)
+
+    # graphs: one context + one captured 32-layer step per cache state, replayed
+    # 1 x state 0, 1 x state 1, 30 x state 2 per block (identical device work)
+    graphs, ctxs = {}, {}
+    side = torch.cuda.Stream(dev)
+    for st in (0, 1, 2):
+        for s in sparse_seqs:
+            s.sparse_state.cache_state = st
+            s.sparse_state.step_in_block = st
+        ctxs[st] = make_ctx(sparse_seqs)
+        step(sparse_seqs, ctxs[st])  # builds and caches the plan outside capture
+        torch.cuda.synchronize()
+        g_ = torch.cuda.CUDAGraph()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g_, stream=side):
+                step(sparse_seqs, ctxs[st])
+        torch.cuda.current_stream().wait_stream(side)
+        graphs[st] = g_
+    rewind()
+    order = [0, 1] + [2] * (blk - 2)
+    graph_cycle_ms = statistics.median(
+        [timed(lambda: [graphs[st].replay() for st in order], 1) for _ in range(max(2, cycles))])
+    graph_dense = torch.cuda.CUDAGraph()
+    ctx_d = make_ctx(dense_seqs)
+    step(dense_seqs, ctx_d)
+    torch.cuda.synchronize()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph_dense, stream=side):
+            step(dense_seqs, ctx_d)
+    torch.cuda.current_stream().wait_stream(side)
+    graph_dense_ms = timed(lambda: graph_dense.replay(), max(2, min(args.steps, 10)))
+    graph_state_ms = {st: timed(lambda: graphs[st].replay(), 3) for st in (0, 1, 2)}
+    if ops.read_device_status(dev) != 0:
+        raise RuntimeError("a kernel reported a device error")
+    sparse_step_ms = statistics.median(cycle_ms) / blk
+    line = {
+        "workload": args.workload, "desc": desc, "n_gpus": world,
+        "parallelism": f"tp{world} head-sharded" if world > 1 else "single GPU",
+        "layers": layers, "heads": [Hq_all, Hkv_all], "batch": B, "seq_lens": [min(lens), max(lens)],
+        "tokens_dense_step": N_full, "retention_ratio": ratio, "n_keep": [min(n_keeps), max(n_keeps)],
+        "eager": {"dense_ms_per_step": dense_ms, "sparse_ms_per_step": sparse_step_ms,
+                  "sparse_speedup_vs_dense": dense_ms / sparse_step_ms},
+        "state_ms": {k: (statistics.median(v) if v else None) for k, v in per_state.items()},
+        "graph": {"dense_ms_per_step": graph_dense_ms,
+                  "sparse_ms_per_step": graph_cycle_ms / blk,
+                  "sparse_speedup_vs_dense": graph_dense_ms / (graph_cycle_ms / blk),
+                  "state_ms": graph_state_ms,
+                  "note": "per-state 32-layer steps captured as CUDA graphs and replayed "
+                          "1x state 0, 1x state 1, 30x state 2 per block"},
+        "dense_attn_tflops": attn_flops(lens, Hq_all) * layers / (graph_dense_ms * 1e-3) / 1e12,
+        "dense_step_tokens_per_s": N_full / (graph_dense_ms * 1e-3),
+        "note": "attention path only (per layer: selection/store, cache gather, varlen attention); "
+                "timed with CUDA events, max over ranks",
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    return 0
+
+
 def run_kernels_case(args):
     """Small profiling case: each native kernel launched 3 times on inputs
     larger than L2 (one c2 layer for attention and the KV store, config-5
@@ -570,6 +785,8 @@ def main():
     ap.add_argument("--skip-extras", action="store_true",
                     help="only the primary timed loop (used for profiling runs)")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
+                    help="c2 = the headline dense step; c3/c4/c5 = sparse diffusion-block cycle")
     ap.add_argument("--kernels-case", action="store_true",
                     help="run each native kernel 3x on a small case (for ncu captures)")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -579,6 +796,8 @@ def main():
     lens = workload_lengths()
     if args.kernels_case:
         return run_kernels_case(args)
+    if args.workload != "c2" and args.impl == "ours":
+        return run_sparse_cycle(args)
     if args.impl == "reference":
         return run_reference_arm(args, lens)
     return run_ours(args, lens)

@@ -229,18 +229,26 @@ cudaError_t launch_select_kv(const SelectArgs& a, bool head_select, int n_seqs, 
   const int nq = head_select ? a.group : a.Hq;
   const size_t smem = select_kv_smem_bytes(nq, a.max_klen);
   dim3 grid(head_select ? a.Hkv : 1, n_seqs);
-  cudaError_t e;
-  if (head_select) {
-    e = cudaFuncSetAttribute(select_kv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
+  // The dynamic-smem opt-in is per device and kernel; raise it only when a
+  // launch needs more than before (so steady-state launches, including ones
+  // recorded into a CUDA graph, make no attribute calls).
+  static size_t smem_set[2][64] = {{0}};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  size_t* have = (dev >= 0 && dev < 64) ? &smem_set[head_select ? 1 : 0][dev] : nullptr;
+  if (have == nullptr || *have < smem) {
+    e = head_select ? cudaFuncSetAttribute(select_kv_kernel<true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                    : cudaFuncSetAttribute(select_kv_kernel<false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    select_kv_kernel<true><<<grid, kThreads, smem, stream>>>(a);
-  } else {
-    e = cudaFuncSetAttribute(select_kv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    if (e != cudaSuccess) return e;
-    select_kv_kernel<false><<<grid, kThreads, smem, stream>>>(a);
+    if (have != nullptr) *have = smem;
   }
+  if (head_select)
+    select_kv_kernel<true><<<grid, kThreads, smem, stream>>>(a);
+  else
+    select_kv_kernel<false><<<grid, kThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -65,6 +65,16 @@ def set_context(
     )
 
 
+def use_context(ctx: Context) -> None:
+    """Install an existing Context object. The attention layers cache the
+    per-step device metadata on the Context, so reinstalling the same object
+    for steps with identical sequence states (e.g. the reuse steps of a
+    diffusion block) skips rebuilding it and keeps CUDA-graph captures free of
+    host-to-device copies."""
+    global _CONTEXT
+    _CONTEXT = ctx
+
+
 def reset_context():
     global _CONTEXT
     _CONTEXT = Context()
