@@ -127,35 +127,39 @@ template <int kPoly>
 DLLM_DEVICE float exp_store_tile(const uint32_t (&s)[4][32], float sl2, float m, uint32_t tS) {
   const f32x2_t sl2x2 = pk2(sl2, sl2);
   const f32x2_t negm2 = pk2(-m, -m);
-  f32x2_t rsa[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
+  const float neg_m = -m;
+  f32x2_t acc2 = pk2(0.f, 0.f);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t pk[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-      const f32x2_t x = ffma2(pk2u(s[c][2 * e], s[c][2 * e + 1]), sl2x2, negm2);
-      f32x2_t p;
       if ((e & 7) < kPoly) {
-        p = exp2_poly2(x);
+        // FMA-pipe pair, packed f32x2 end to end
+        const f32x2_t x = ffma2(pk2u(s[c][2 * e], s[c][2 * e + 1]), sl2x2, negm2);
+        const f32x2_t p = exp2_poly2(x);
+        acc2 = fadd2(acc2, p);
+        float p0, p1;
+        upk2(p, p0, p1);
+        pk[e] = pack_bf16x2(p0, p1);
       } else {
-        float x0, x1;
-        upk2(x, x0, x1);
-        p = pk2(ex2_approx(x0), ex2_approx(x1));
+        // MUFU pair with scalar arithmetic (no pair packing around MUFU)
+        const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
+        acc[(2 * e) & 3] += p0;
+        acc[(2 * e + 1) & 3] += p1;
+        pk[e] = pack_bf16x2(p0, p1);
       }
-      rsa[e & 1] = fadd2(rsa[e & 1], p);
-      float p0, p1;
-      upk2(p, p0, p1);
-      pk[e] = pack_bf16x2(p0, p1);
     }
     tmem_st16(tS + c * 16, pk);
 #ifdef DLLM_TRACE
     if ((threadIdx.x & 127) == 0) trace_rec(trace_err, 17 + c, 0, 0);
 #endif
   }
-  float r0, r1, r2, r3;
-  upk2(rsa[0], r0, r1);
-  upk2(rsa[1], r2, r3);
-  return (r0 + r1) + (r2 + r3);
+  float a0, a1;
+  upk2(acc2, a0, a1);
+  return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + (a0 + a1);
 }
 
 }  // namespace
@@ -263,24 +267,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 8 || warp == 10) {
     // ------------------------------------------------------------------ TMA
     // warp 8: Q and K tiles; warp 10: V tiles (independent rings, so a wait
-    // for a free V stage never holds back a K load and vice versa).
-    if (lane == 0) {
-      const bool kq = warp == 8;
-      const uint64_t pol_q = policy_evict_first();
-      const uint64_t pol_kv = policy_evict_last();
-      const int nst = kq ? kStagesK : kStagesV;
-      const int bfull = kq ? BAR_KFULL : BAR_VFULL;
-      const int bempty = kq ? BAR_KEMPTY : BAR_VEMPTY;
-      const uint32_t ring = base + (kq ? kOffK : kOffV);
-      uint32_t q_it = 0;     // units whose Q was loaded (warp 8)
-      uint32_t done = 0;     // tiles issued into this ring
-      bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        const Unit t = decode_unit(u, args);
-        if (!t.valid) continue;
-        if (kq) {
-          if (q_it > 0) ok = mbar_wait(bar(BAR_QEMPTY), (q_it - 1) & 1, abort_flag);
-          if (!ok) break;
+    // for a free V stage never holds back a K load and vice versa). The whole
+    // warp walks the loop (uniformly); lane 0 issues the TMA copies and the
+    // barrier operations, all lanes help with paged cached tiles.
+    const bool kq = warp == 8;
+    const uint64_t pol_q = policy_evict_first();
+    const uint64_t pol_kv = policy_evict_last();
+    const int nst = kq ? kStagesK : kStagesV;
+    const int bfull = kq ? BAR_KFULL : BAR_VFULL;
+    const int bempty = kq ? BAR_KEMPTY : BAR_VEMPTY;
+    const uint32_t ring = base + (kq ? kOffK : kOffV);
+    const __nv_bfloat16* cache = kq ? args.kc : args.vc;
+    uint32_t q_it = 0;     // units whose Q was loaded (warp 8)
+    uint32_t done = 0;     // tiles issued into this ring
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      const Unit t = decode_unit(u, args);
+      if (!t.valid) continue;
+      if (kq) {
+        if (q_it > 0) ok = mbar_wait(bar(BAR_QEMPTY), (q_it - 1) & 1, abort_flag);
+        if (!ok) break;
+        if (lane == 0) {
           mbar_arrive_expect_tx(bar(BAR_Q), t.ntiles * kTileBytes);
           for (int i = 0; i < t.ntiles; ++i) {
             const uint32_t dst = base + kOffQ + i * kTileBytes;
@@ -288,28 +295,76 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(dst, &tmQ, bar(BAR_Q), 0, t.hq, row, pol_q);
             tma_load_3d(dst + kChunkBytes, &tmQ, bar(BAR_Q), 64, t.hq, row, pol_q);
           }
-          ++q_it;
         }
-        for (int j = 0; j < t.nkv; ++j) {
-          const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+        ++q_it;
+      }
+      for (int j = 0; j < t.nkv; ++j) {
+        const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+        const int st = done % nst;
+        if (done >= (uint32_t)nst) ok = mbar_wait(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
+        if (!ok) break;
+        const uint32_t dk = ring + st * kTileBytes;
+        if (kt.seg == 0 && args.slots != nullptr) {
+          // Paged cached tile: rows slots[row0 .. row0+valid) of the cache.
+          // Consecutive slots (the page layout the model runner produces)
+          // become one TMA copy of the cache; anything else is gathered by
+          // the warp with bounds-checked 16-byte loads.
+          const int32_t* sp = args.slots + kt.row0;
+          const int s0 = sp[0];
+          int sl[4];
+          bool contig = s0 >= 0 && (int64_t)s0 + kt.valid <= args.num_slots;
+#pragma unroll
+          for (int r4 = 0; r4 < 4; ++r4) {
+            const int r = lane + 32 * r4;
+            sl[r4] = r < kt.valid ? sp[r] : -1;
+            if (r < kt.valid && sl[r4] != s0 + r) contig = false;
+          }
+          contig = __all_sync(0xffffffffu, contig);
+          if (contig) {
+            if (lane == 0) {
+              const CUtensorMap* mp = kq ? &tmKc : &tmVc;
+              mbar_arrive_expect_tx(bar(bfull + st), kTileBytes);
+              tma_load_3d(dk, mp, bar(bfull + st), 0, t.hkv, s0, pol_kv);
+              tma_load_3d(dk + kChunkBytes, mp, bar(bfull + st), 64, t.hkv, s0, pol_kv);
+            }
+          } else {
+            uint8_t* tile = smem + (dk - base);
+#pragma unroll 1
+            for (int r4 = 0; r4 < 4; ++r4) {
+              const int r = lane + 32 * r4;
+              const int64_t slot = sl[r4];
+              const bool in_range = slot >= 0 && slot < args.num_slots;
+              if (r < kt.valid && !in_range) set_error(args.err, kDevSlotOutOfRange);
+              const uint4* src = reinterpret_cast<const uint4*>(
+                  cache + (in_range ? slot : 0) * args.c_tok_stride + (int64_t)t.hkv * kD);
+#pragma unroll
+              for (int c16 = 0; c16 < 16; ++c16) {
+                uint4 val = make_uint4(0, 0, 0, 0);
+                if (r < kt.valid && in_range) val = __ldg(src + c16);
+                // SW128 layout: 16-byte unit index XOR (row mod 8) inside each 64-column half
+                const uint32_t off = (c16 >> 3) * kChunkBytes + r * 128 + (((c16 & 7) ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4*>(tile + off) = val;
+              }
+            }
+            fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(bfull + st));
+          }
+        } else if (lane == 0) {
           const CUtensorMap* mp = kq ? (kt.seg == 0 ? &tmKc : &tmK) : (kt.seg == 0 ? &tmVc : &tmV);
-          const int st = done % nst;
-          if (done >= (uint32_t)nst) ok = mbar_wait(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
-          if (!ok) break;
-          const uint32_t dk = ring + st * kTileBytes;
           mbar_arrive_expect_tx(bar(bfull + st), kTileBytes);
           tma_load_3d(dk, mp, bar(bfull + st), 0, t.hkv, kt.row0, pol_kv);
           tma_load_3d(dk + kChunkBytes, mp, bar(bfull + st), 64, t.hkv, kt.row0, pol_kv);
-          ++done;
-          TRACE(kq ? 2 : 3, j, 0);
         }
+        ++done;
+        if (lane == 0) TRACE(kq ? 2 : 3, j, 0);
       }
-      if (*abort_flag) {
-        // Drain: wait (bounded) for the loads that may still be in flight.
-        if (kq && q_it > 0) mbar_wait_drain(bar(BAR_Q), (q_it - 1) & 1, 100000000ull);
-        for (uint32_t n = (done > (uint32_t)nst ? done - nst : 0); n < done; ++n)
-          mbar_wait_drain(bar(bfull + n % nst), (n / nst) & 1, 100000000ull);
-      }
+    }
+    if (lane == 0 && *abort_flag) {
+      // Drain: wait (bounded) for the loads that may still be in flight.
+      if (kq && q_it > 0) mbar_wait_drain(bar(BAR_Q), (q_it - 1) & 1, 100000000ull);
+      for (uint32_t n = (done > (uint32_t)nst ? done - nst : 0); n < done; ++n)
+        mbar_wait_drain(bar(bfull + n % nst), (n / nst) & 1, 100000000ull);
     }
     __syncwarp();
   } else if (warp == 9) {

@@ -22,6 +22,13 @@ struct AttnKernelArgs {
   int group;               // Hq / Hkv
   float scale_log2;        // softmax_scale * log2(e)
   int32_t* err;            // optional device status word
+  // Paged cached segment (optional): when `slots` is set, the cached rows of
+  // sequence b are cache rows slots[cu_c[b] .. cu_c[b+1]) of kc/vc.
+  const int32_t* slots;
+  int64_t num_slots;
+  const __nv_bfloat16* kc;
+  const __nv_bfloat16* vc;
+  int64_t c_tok_stride;    // elements between cache slots
   int qpairs;              // 256-row query tile pairs per (sequence, head); set by the launcher
   int total_units;         // B * Hq * qpairs; set by the launcher
 };

@@ -96,12 +96,16 @@ int check_rows(const char* name, const void* p, int64_t tok_stride, int heads, i
   return DLLM_OK;
 }
 
+// kc/vc are either row tensors of total_c rows (slots == nullptr) or paged
+// caches of total_c = num_slots slots addressed through `slots` (cu_c then
+// indexes the slot list).
 int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
                 const void* v, int64_t v_tok_stride, const void* kc, int64_t kc_tok_stride,
                 const void* vc, int64_t vc_tok_stride, void* o, int64_t o_tok_stride,
                 const int32_t* cu_q, const int32_t* cu_k, const int32_t* cu_c, int batch,
                 int max_q, int64_t total_q, int64_t total_k, int64_t total_c, int Hq, int Hkv,
-                int head_dim, float scale, int32_t* err, void* stream) {
+                int head_dim, float scale, int32_t* err, void* stream,
+                const int32_t* slots = nullptr) {
   if (head_dim != 128)
     return fail(DLLM_ERR_UNSUPPORTED, "head_dim %d not supported (only 128)", head_dim);
   if (Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
@@ -120,6 +124,8 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   if (cu_c != nullptr) {
     if ((rc = check_rows("k_cached", kc, kc_tok_stride, Hkv, total_c)) != DLLM_OK) return rc;
     if ((rc = check_rows("v_cached", vc, vc_tok_stride, Hkv, total_c)) != DLLM_OK) return rc;
+    if (slots != nullptr && kc_tok_stride != vc_tok_stride)
+      return fail(DLLM_ERR_INVALID_ARG, "k_cache and v_cache slot strides differ");
   }
   CUtensorMap tq, tk, tv, tkc, tvc;
   const int kv_rows = dllm::attn_fwd_kv_rows_per_tile();
@@ -147,6 +153,11 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.group = Hq / Hkv;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
+  a.slots = slots;
+  a.num_slots = slots != nullptr ? total_c : 0;
+  a.kc = reinterpret_cast<const __nv_bfloat16*>(kc);
+  a.vc = reinterpret_cast<const __nv_bfloat16*>(vc);
+  a.c_tok_stride = kc_tok_stride;
   a.qpairs = 0;
   a.total_units = 0;
   cudaError_t e = dllm::launch_attn_fwd(tq, tk, tv, tkc, tvc, a, max_q, num_sms_of_current_device(),
@@ -242,6 +253,24 @@ int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, const void*
                      vc_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k, cu_seqlens_c,
                      batch, max_seqlen_q, total_q, total_k, total_c, num_heads, num_kv_heads,
                      head_dim, softmax_scale, err_flag, stream);
+}
+
+int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, const void* k,
+                               int64_t k_tok_stride, const void* v, int64_t v_tok_stride,
+                               const void* k_cache, const void* v_cache, int64_t cache_tok_stride,
+                               int64_t num_slots, const int32_t* slots,
+                               const int32_t* cu_seqlens_slots, void* o, int64_t o_tok_stride,
+                               const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
+                               int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
+                               int num_kv_heads, int head_dim, float softmax_scale,
+                               int32_t* err_flag, void* stream) {
+  if (cu_seqlens_slots == nullptr || slots == nullptr)
+    return fail(DLLM_ERR_INVALID_ARG, "slots / cu_seqlens_slots is null");
+  if (num_slots <= 0) return fail(DLLM_ERR_INVALID_ARG, "num_slots must be > 0");
+  return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, k_cache, cache_tok_stride,
+                     v_cache, cache_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k,
+                     cu_seqlens_slots, batch, max_seqlen_q, total_q, total_k, num_slots, num_heads,
+                     num_kv_heads, head_dim, softmax_scale, err_flag, stream, slots);
 }
 
 int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,

@@ -43,6 +43,11 @@ SIGNATURES = {
          _I64, _I, _I, _I, _F, _P, _P],
         _I,
     ),
+    "dllm_attn_varlen_paged_fwd": (
+        [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _I, _I, _I64,
+         _I64, _I, _I, _I, _F, _P, _P],
+        _I,
+    ),
     "dllm_select_kv_store": (
         [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _I64, _P, _P, _P, _P],
         _I,

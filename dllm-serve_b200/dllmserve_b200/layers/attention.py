@@ -9,10 +9,10 @@ reference's argument order and assertions (attention.py:33-92).
 
 The diffusion path (``context.is_diffusion``, attention.py:150-306) runs as
   1. one scoring/top-k/store launch per ``head_select`` flavour for the
-     sequences in the "compute cache" state (state 1),
-  2. one gather of the cached rows of "reuse" sequences (state 2), and
-  3. one non-causal varlen attention launch over every sequence, whose keys
-     are [cached rows ; fresh rows] for state-2 sequences,
+     sequences in the "compute cache" state (state 1), and
+  2. one non-causal varlen attention launch over every sequence, whose keys
+     are [cached rows read from the paged cache by slot ; fresh rows] for
+     "reuse" sequences (state 2),
 with all per-sequence metadata built once per step (``StepPlan``).
 """
 from __future__ import annotations
@@ -105,10 +105,10 @@ class Attention(nn.Module):
                                 self.k_cache, self.v_cache, slots, top_idx)
         out = torch.empty((q.shape[0], self.num_heads, self.head_dim), dtype=q.dtype, device=dev)
         if plan.total_c > 0:
-            kc, vc = plan.cached_buffers(self.num_kv_heads, self.head_dim, k.dtype, dev)
-            load_kvcache(kc, vc, self.k_cache, self.v_cache, plan.slots_c)
+            # reuse state: cached rows read straight from the paged cache
             ops.varlen_attention(q, k, v, plan.cu, plan.cu, plan.max_rows, self.scale,
-                                 k_cached=kc, v_cached=vc, cu_seqlens_c=plan.cu_c, out=out)
+                                 k_cache=self.k_cache, v_cache=self.v_cache, slots=plan.slots_c,
+                                 cu_seqlens_slots=plan.cu_c, out=out)
         else:
             ops.varlen_attention(q, k, v, plan.cu, plan.cu, plan.max_rows, self.scale, out=out)
         return out.view(-1, self.num_heads * self.head_dim)

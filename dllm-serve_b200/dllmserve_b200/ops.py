@@ -134,10 +134,16 @@ def varlen_attention(
     k_cached: torch.Tensor | None = None,
     v_cached: torch.Tensor | None = None,
     cu_seqlens_c: torch.Tensor | None = None,
+    k_cache: torch.Tensor | None = None,
+    v_cache: torch.Tensor | None = None,
+    slots: torch.Tensor | None = None,
+    cu_seqlens_slots: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Non-causal varlen attention (bf16). With ``k_cached``/``v_cached``/
-    ``cu_seqlens_c`` each sequence attends to [cached rows ; fresh rows]."""
+    ``cu_seqlens_c`` each sequence attends to [cached rows ; fresh rows]; with
+    ``k_cache``/``v_cache``/``slots``/``cu_seqlens_slots`` the cached rows are
+    read straight from the paged cache (slots[cu[b]:cu[b+1]] for sequence b)."""
     Hq, D = q.shape[1], q.shape[2]
     Hkv = k.shape[1]
     _check_rows("q", q, Hq, D)
@@ -161,7 +167,27 @@ def varlen_attention(
     lib = _native.lib()
     status = device_status_word(dev).data_ptr()
     with torch.cuda.device(dev):
-        if k_cached is None:
+        if k_cache is not None:
+            _require_cuda(q, k_cache, v_cache, slots, cu_seqlens_slots)
+            if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+                raise ValueError("caches must be bfloat16")
+            row = Hkv * D
+            if (k_cache.stride(-1) != 1 or k_cache.numel() % row or v_cache.numel() != k_cache.numel()
+                    or not k_cache.is_contiguous() or not v_cache.is_contiguous()):
+                raise ValueError("caches must be contiguous [blocks, block_size, num_kv_heads, head_dim]")
+            for name, c in (("slots", slots), ("cu_seqlens_slots", cu_seqlens_slots)):
+                if c.dtype != torch.int32 or not c.is_contiguous():
+                    raise ValueError(f"{name} must be contiguous int32")
+            if cu_seqlens_slots.numel() != B + 1:
+                raise ValueError("cu_seqlens_slots must have batch+1 entries")
+            rc = lib.dllm_attn_varlen_paged_fwd(
+                q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row,
+                slots.data_ptr(), cu_seqlens_slots.data_ptr(), out.data_ptr(), out.stride(0),
+                cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), B, int(max_seqlen_q), q.shape[0],
+                k.shape[0], Hq, Hkv, D, float(softmax_scale), status, _stream_ptr(),
+            )
+        elif k_cached is None:
             rc = lib.dllm_attn_varlen_fwd(
                 q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
                 out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),

@@ -11,6 +11,9 @@
  *   dllm_attn_varlen_cached_fwd
  *                             <- reuse-state K/V assembly + varlen call (attention.py:235-299):
  *                                keys are [cached selected rows ; fresh block rows]
+ *   dllm_attn_varlen_paged_fwd
+ *                             <- the same with the cached rows read from the paged cache by
+ *                                slot (load_kvcache fused in, attention.py:241-263)
  *   dllm_select_kv_store      <- _select_important_head_kv (attention.py:344-413) or
  *                                _select_important_kv (attention.py:308-342), followed by
  *                                the k_prefix_suffix[idx] gather and store_kvcache of the
@@ -122,6 +125,27 @@ DLLM_API int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, co
                                 int64_t total_q, int64_t total_k, int64_t total_c,
                                 int num_heads, int num_kv_heads, int head_dim,
                                 float softmax_scale, int32_t* err_flag, void* stream);
+
+/*
+ * As dllm_attn_varlen_cached_fwd, but the cached keys/values of sequence b are read
+ * straight from the paged KV cache: rows slots[cu_seqlens_slots[b] .. cu_seqlens_slots[b+1])
+ * of k_cache / v_cache (num_slots slots, cache_tok_stride elements apart, the layout of
+ * model_runner.py:192-206). Replaces zeros + load_kvcache + torch.cat of the reuse state
+ * (attention.py:241-263) and the varlen call (:289-299) with one launch. Runs of 128
+ * consecutive slots (the runner's 256-token pages) are copied with TMA; other slot lists are
+ * gathered row by row. Slots outside [0, num_slots) read as zero rows and flag
+ * DLLM_DEV_SLOT_OUT_OF_RANGE. Cache rows must hold finite values (the reference allocates
+ * the cache with torch.zeros).
+ */
+DLLM_API int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, const void* k,
+                               int64_t k_tok_stride, const void* v, int64_t v_tok_stride,
+                               const void* k_cache, const void* v_cache, int64_t cache_tok_stride,
+                               int64_t num_slots, const int32_t* slots,
+                               const int32_t* cu_seqlens_slots, void* o, int64_t o_tok_stride,
+                               const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
+                               int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
+                               int num_kv_heads, int head_dim, float softmax_scale,
+                               int32_t* err_flag, void* stream);
 
 /*
  * Per-sequence descriptor for dllm_select_kv_store: 8 int32 values per sequence.

@@ -320,3 +320,63 @@ def test_select_kv_store_bit_exact(dev, case):
         got = top[d[6]:d[6] + n * (hkv if hs else 1)]
         assert np.array_equal(got.reshape(ri.shape), ri)
     assert torch.equal(kc.cpu().float(), kc_ref) and torch.equal(vc.cpu().float(), vc_ref)
+
+
+@pytest.mark.parametrize("layout", ["pages", "random", "mixed"])
+@pytest.mark.parametrize("hq,hkv", [(4, 4), (7, 1)])
+def test_attention_paged_cache(dev, layout, hq, hkv):
+    """keys = [cache rows at slots ; fresh rows], read straight from the paged cache
+    (TMA for runs of consecutive slots, warp gather otherwise)."""
+    g = I.gen(90 + hq + len(layout))
+    D, pages = 128, 12
+    lq = [32, 32, 17, 64]
+    n_c = [304, 0, 129, 300]
+    kc = I.normal(g, (pages, 256, hkv, D))
+    vc = I.normal(g, (pages, 256, hkv, D))
+    order = torch.randperm(pages, generator=g).tolist()
+    slot_lists, off = [], 0
+    for i, n in enumerate(n_c):
+        if layout == "random" or (layout == "mixed" and i % 2 == 1):
+            lst = torch.randperm(pages * 256, generator=g)[:n].tolist()
+        else:
+            npg = (n + 255) // 256
+            lst = []
+            for j, p in enumerate(order[off:off + npg]):
+                lst.extend(range(p * 256, p * 256 + min(256, n - j * 256)))
+            off += npg
+        slot_lists.append(torch.tensor(lst, dtype=torch.int32))
+    slots = torch.cat(slot_lists)
+    q = I.normal(g, (sum(lq), hq, D))
+    k, v = I.normal(g, (sum(lq), hkv, D)), I.normal(g, (sum(lq), hkv, D))
+    kg, vg = R.load_kvcache(kc, vc, slots, hkv, D)
+    ref = R.varlen_attention(q, k, v, _cu(lq), _cu(lq), D ** -0.5, kg, vg, _cu(n_c))
+    t = lambda x: x.to(dev, torch.bfloat16)
+    cq = torch.tensor(_cu(lq), dtype=torch.int32, device=dev)
+    cs = torch.tensor(_cu(n_c), dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(t(q), t(k), t(v), cq, cq, max(lq), D ** -0.5,
+                                  k_cache=t(kc), v_cache=t(vc), slots=slots.to(dev),
+                                  cu_seqlens_slots=cs)
+    _check_attn(out, ref, f"{layout} hq={hq} hkv={hkv}")
+    _status_clear(dev)
+
+
+def test_attention_paged_out_of_range_slot(dev):
+    """An out-of-range slot reads as a zero key/value row and flags the status word."""
+    g = I.gen(95)
+    D, H = 128, 2
+    kc = I.normal(g, (2, 256, H, D))
+    vc = I.normal(g, (2, 256, H, D))
+    slots = torch.tensor([3, 700, 5], dtype=torch.int32)  # 700 >= 512 slots
+    q, k, v = I.normal(g, (4, H, D)), I.normal(g, (4, H, D)), I.normal(g, (4, H, D))
+    kg, vg = R.load_kvcache(kc, vc, torch.tensor([3, 0, 5]), H, D)
+    kg[1] = 0
+    vg[1] = 0
+    ref = R.varlen_attention(q, k, v, [0, 4], [0, 4], D ** -0.5, kg, vg, [0, 3])
+    t = lambda x: x.to(dev, torch.bfloat16)
+    c4 = torch.tensor([0, 4], dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(t(q), t(k), t(v), c4, c4, 4, D ** -0.5, k_cache=t(kc),
+                                  v_cache=t(vc), slots=slots.to(dev),
+                                  cu_seqlens_slots=torch.tensor([0, 3], dtype=torch.int32, device=dev))
+    torch.cuda.synchronize()
+    assert _ops().read_device_status(dev) == 1
+    _check_attn(out, ref)
