@@ -158,6 +158,28 @@ def test_attention_separate_q_and_k_lengths(dev):
     _check_attn(out, ref)
 
 
+@pytest.mark.parametrize("batch", [256, 300])
+def test_attention_many_sequences(dev, batch):
+    """Batches up to 256 sequences use the cost-ranked unit schedule, larger
+    ones the natural order; empty query or key segments included."""
+    g = I.gen(90 + batch)
+    D, hq, hkv = 128, 2, 1
+    lq = torch.randint(0, 300, (batch,), generator=g).tolist()
+    lk = torch.randint(0, 300, (batch,), generator=g).tolist()
+    lq[3], lk[5], lq[7], lk[7] = 0, 0, 0, 0
+    q = I.normal(g, (sum(lq), hq, D))
+    k, v = I.normal(g, (sum(lk), hkv, D)), I.normal(g, (sum(lk), hkv, D))
+    ref = R.varlen_attention(q, k, v, _cu(lq), _cu(lk), D ** -0.5)
+    t = lambda x: x.to(dev, torch.bfloat16)
+    out = torch.full((sum(lq), hq, D), float("nan"), dtype=torch.bfloat16, device=dev)
+    _ops().varlen_attention(t(q), t(k), t(v), torch.tensor(_cu(lq), dtype=torch.int32, device=dev),
+                            torch.tensor(_cu(lk), dtype=torch.int32, device=dev), max(lq),
+                            D ** -0.5, out=out)
+    torch.cuda.synchronize()
+    _check_attn(out, ref, f"batch={batch}")
+    _status_clear(dev)
+
+
 def test_attention_fused_qkv_views(dev):
     """q/k/v as strided views of one fused projection output."""
     g = I.gen(78)
