@@ -172,15 +172,15 @@ struct Unit {
   int k_begin, nk, c_begin, nc, nkv;
 };
 
-// Units are numbered ((b * Hq) + hq) * qpairs + p, so consecutive units share
+// Units are numbered ((b * Hq) + hq) * qunits + p, so consecutive units share
 // a sequence and head (their K/V stay hot in L2 while several CTAs read them).
 DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
   Unit r;
-  const int per_b = a.Hq * a.qpairs;
+  const int per_b = a.Hq * a.qunits;
   const int b = u / per_b;
   const int rem = u - b * per_b;
-  r.hq = rem / a.qpairs;
-  const int p = rem - r.hq * a.qpairs;
+  r.hq = rem / a.qunits;
+  const int p = rem - r.hq * a.qunits;
   r.hkv = r.hq / a.group;
   r.q_begin = a.cu_q[b];
   r.Lq = a.cu_q[b + 1] - r.q_begin;
@@ -637,8 +637,8 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, cons
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   AttnKernelArgs a = args;
-  a.qpairs = (max_q + 2 * kTileM - 1) / (2 * kTileM);
-  const long long units = (long long)a.B * a.Hq * a.qpairs;
+  a.qunits = (max_q + 2 * kTileM - 1) / (2 * kTileM);
+  const long long units = (long long)a.B * a.Hq * a.qunits;
   if (units == 0) return cudaSuccess;
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_units = (int)units;

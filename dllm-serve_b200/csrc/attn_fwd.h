@@ -29,16 +29,27 @@ struct AttnKernelArgs {
   const __nv_bfloat16* kc;
   const __nv_bfloat16* vc;
   int64_t c_tok_stride;    // elements between cache slots
-  int qpairs;              // 256-row query tile pairs per (sequence, head); set by the launcher
-  int total_units;         // B * Hq * qpairs; set by the launcher
+  int qunits;              // query units per (sequence, head): 256-row tile pairs (pair
+                           // kernel) or 128-row tiles (split kernel); set by the launcher
+  int total_units;         // B * Hq * qunits; set by the launcher
 };
 
 uint32_t attn_fwd_smem_bytes();
 int attn_fwd_kv_rows_per_tile();  // rows of a key/value TMA box
 
+// "Pair" kernel (attn_fwd.cu): a unit is two 128-row query tiles, one per
+// softmax warpgroup. Used when some query segment is longer than 128 rows.
 cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                             const CUtensorMap& tmKc, const CUtensorMap& tmVc,
                             const AttnKernelArgs& args, int max_q, int num_sms,
                             cudaStream_t stream);
+
+// "Split" kernel (attn_fwd_split.cu): a unit is one 128-row query tile and the
+// two softmax warpgroups split each KV tile's columns. Used when max_q <= 128.
+constexpr int kSplitMaxQ = 128;
+cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                  const CUtensorMap& tmV, const CUtensorMap& tmKc,
+                                  const CUtensorMap& tmVc, const AttnKernelArgs& args, int max_q,
+                                  int num_sms, cudaStream_t stream);
 
 }  // namespace dllm

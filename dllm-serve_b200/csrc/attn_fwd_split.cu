@@ -1,0 +1,714 @@
+// Non-causal varlen flash-attention forward for sm_100a (tcgen05 + TMEM + TMA),
+// "split" variant for launches whose query segments fit one 128-row tile
+// (max_seqlen_q <= 128: the reuse steps' fresh blocks). The "pair" kernel in
+// attn_fwd.cu gives each unit two query tiles; here a unit has one, and the
+// two softmax warpgroups split every KV tile's columns instead, so neither
+// sits idle on a lone tile.
+//
+// Replaces the `flash_attn_varlen_func(..., causal=False)` call of the
+// reference's diffusion attention (dllmserve/layers/attention.py:289-299),
+// including the cached-K/V ("reuse") sequences whose keys are the selected
+// cached rows followed by the block's fresh rows (attention.py:235-265).
+//
+// Persistent kernel: one CTA per SM loops over work units = (sequence b,
+// query head h, 128-row query tile). Roles inside the CTA (11 warps):
+//   warps 0-3  softmax warpgroup 0: kv rows 0-63 of every KV tile
+//   warps 4-7  softmax warpgroup 1: kv rows 64-127 of every KV tile
+//   warp  8    TMA producer: Q tiles (2-deep ring) and the K ring
+//   warp  9    MMA issuer (also allocates / frees TMEM)
+//   warp  10   TMA producer: the V ring
+// Both warpgroups own all 128 query rows (TMEM lanes) and split each KV
+// tile's 128 columns; each keeps its own running max / sum and its own
+// output accumulator, and the two partial results are merged once per unit.
+// TMEM (512 columns): S buffers SB0 [0,128) and SB1 [128,256) (KV tile j
+// uses SB(j mod 2)), O_a [256,384) (kv rows 0-63 of every tile), O_b
+// [384,512) (kv rows 64-127). Warpgroup w writes its bf16 P half over the
+// first 32 columns of its own S half (SB + 64w). MMA issue order per tile j:
+//   PV_a(j), PV_b(j), QK(j+2) -> SB(j mod 2)
+// so QK(j+1) has filled the other S buffer while the softmax works on tile
+// j, and QK(j+2) overwrites P(j) only after the PVs that read it (tcgen05
+// MMAs of one thread execute in order).
+//
+// Each KV sequence is the concatenation of up to two segments:
+//   segment 0: cached rows (k_cache/v_cache gathered rows, `cu_c`), optional
+//   segment 1: fresh rows of the step's k/v (`cu_k`)
+// KV tiles never straddle segments; a partial tile uses a smaller MMA N.
+#include "common.cuh"
+#include "attn_fwd.h"
+
+namespace dllm {
+namespace split {
+
+namespace {
+
+constexpr int kD = 128;          // head dim (only 128 is instantiated)
+constexpr int kTileM = 128;      // query rows per unit
+constexpr int kTileN = 128;      // kv rows per tile
+constexpr int kHalfN = 64;       // kv rows per softmax warpgroup
+constexpr int kStagesQ = 2;      // Q ring depth (the next unit's Q loads early)
+constexpr int kStagesK = 3;      // K ring depth (QK runs two tiles ahead of PV)
+constexpr int kStagesV = 2;      // V ring depth
+constexpr int kThreads = 352;
+
+// Softmax code-shape switch (tuning; default is the measured best).
+#ifndef DLLM_SM_POLY
+#define DLLM_SM_POLY 0
+#endif
+constexpr int kSmPoly = DLLM_SM_POLY;         // pairs of 8 evaluated on the FMA pipe
+constexpr uint32_t kTileBytes = kTileM * kD * 2;  // 32 KB (bf16)
+constexpr uint32_t kChunkBytes = 128 * 128;       // 128 rows x 128 B (64 bf16)
+
+// Shared-memory map (offsets from a 1024-aligned base).
+constexpr uint32_t kOffQ = 0;                                   // kStagesQ tiles
+constexpr uint32_t kOffK = kOffQ + kStagesQ * kTileBytes;       // kStagesK tiles
+constexpr uint32_t kOffV = kOffK + kStagesK * kTileBytes;       // kStagesV tiles
+constexpr uint32_t kOffBar = kOffV + kStagesV * kTileBytes;     // barriers
+
+// barrier indices
+constexpr int BAR_QFULL = 0;
+constexpr int BAR_QEMPTY = BAR_QFULL + kStagesQ;
+constexpr int BAR_KFULL = BAR_QEMPTY + kStagesQ;
+constexpr int BAR_KEMPTY = BAR_KFULL + kStagesK;
+constexpr int BAR_VFULL = BAR_KEMPTY + kStagesK;
+constexpr int BAR_VEMPTY = BAR_VFULL + kStagesV;
+constexpr int BAR_SFULL = BAR_VEMPTY + kStagesV;  // 2: S buffer holds QK of a tile
+constexpr int BAR_PFULL = BAR_SFULL + 2;          // 2: both P halves of a buffer written
+constexpr int BAR_OREADY = BAR_PFULL + 2;         // 1: PVs of one more tile completed
+constexpr int BAR_OFULL = BAR_OREADY + 1;         // 1: a unit's last PVs completed
+constexpr int BAR_XML = BAR_OFULL + 1;            // 1: warpgroup 1's (max, sum) published
+constexpr int BAR_XF = BAR_XML + 1;               // 1: the merge factors published
+constexpr int BAR_DRAIN = BAR_XF + 1;             // 1
+constexpr uint32_t kNumBars = BAR_DRAIN + 1;
+constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;           // abort flag, TMEM address
+constexpr uint32_t kOffXch = kOffMisc + 64;                     // float2 per query row
+constexpr uint32_t kSmemBytes = kOffXch + kTileM * 8 + 1024;    // + alignment slack
+static_assert(kSmemBytes <= 232448, "over the sm_100a per-CTA shared-memory limit");
+
+DLLM_DEVICE int row_in_tile_of(int tid) { return tid & 127; }
+
+struct KvTile {
+  int seg;    // 0 = cached, 1 = fresh
+  int row0;   // first row in the segment's source tensor
+  int valid;  // valid rows in this tile (1..128)
+};
+
+// Tile t of a sequence whose cached segment has nc rows starting at c0 and
+// fresh segment nk rows starting at k0.
+DLLM_DEVICE KvTile kv_tile(int t, int nc, int c0, int nk, int k0) {
+  int tc = (nc + kTileN - 1) / kTileN;
+  KvTile r;
+  if (t < tc) {
+    r.seg = 0;
+    r.row0 = c0 + t * kTileN;
+    r.valid = min(kTileN, nc - t * kTileN);
+  } else {
+    int u = t - tc;
+    r.seg = 1;
+    r.row0 = k0 + u * kTileN;
+    r.valid = min(kTileN, nk - u * kTileN);
+  }
+  return r;
+}
+
+#ifdef DLLM_TRACE
+// Debug-only event trace (never built into the shipped library): for every
+// 256th CTA (up to 16) each warp records (clock64, code) pairs into its own
+// slice after the status word; per-warp counters live in shared memory.
+__shared__ unsigned g_trace_cnt[16];
+DLLM_DEVICE void trace_rec(int32_t* err, int ev, int j, int tile) {
+  const unsigned cid = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (err == nullptr || (cid & 255u) != 0 || (cid >> 8) >= 16) return;
+  const int w = threadIdx.x >> 5;
+  const unsigned k = atomicAdd(&g_trace_cnt[w], 1u);
+  if (k >= 1024) return;
+  unsigned long long* region =
+      reinterpret_cast<unsigned long long*>(err + 16) + ((cid >> 8) * 16 + w) * 2048;
+  long long clk;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(clk));
+  region[2 * k] = (unsigned long long)clk;
+  region[2 * k + 1] = (unsigned long long)(ev | (j << 8) | (tile << 20) | (w << 24));
+}
+#define TRACE(ev, j, tile) trace_rec(args.err, ev, j, tile)
+__device__ int32_t* trace_err;
+#else
+#define TRACE(ev, j, tile) \
+  do {                     \
+  } while (0)
+#endif
+
+
+
+// P = 2^(S*scale_log2 - m) for one row of a 64-column half tile (two chunks
+// of 32 columns), packed to bf16 pairs and stored to TMEM at tP (chunk c ->
+// columns 16c .. 16c+15); returns the row sum of P (fp32). kPoly of every 8
+// column pairs use the FMA-pipe exp2, the rest MUFU ex2 (the split is fixed
+// at compile time so no path is evaluated twice).
+template <int kPoly>
+DLLM_DEVICE float exp_store_half(const uint32_t (&s)[2][32], float sl2, float m, uint32_t tP) {
+  const f32x2_t sl2x2 = pk2(sl2, sl2);
+  const f32x2_t negm2 = pk2(-m, -m);
+  const float neg_m = -m;
+  f32x2_t acc2 = pk2(0.f, 0.f);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if ((e & 7) < kPoly) {
+        const f32x2_t x = ffma2(pk2u(s[c][2 * e], s[c][2 * e + 1]), sl2x2, negm2);
+        const f32x2_t p = exp2_poly2(x);
+        acc2 = fadd2(acc2, p);
+        float p0, p1;
+        upk2(p, p0, p1);
+        pk[e] = pack_bf16x2(p0, p1);
+      } else {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
+        acc[(2 * e) & 3] += p0;
+        acc[(2 * e + 1) & 3] += p1;
+        pk[e] = pack_bf16x2(p0, p1);
+      }
+    }
+    tmem_st16(tP + c * 16, pk);
+  }
+  float a0, a1;
+  upk2(acc2, a0, a1);
+  return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + (a0 + a1);
+}
+
+}  // namespace
+
+// One work unit: (sequence b, query head hq, 128-row query tile).
+struct Unit {
+  bool valid;
+  int hq, hkv;
+  int q_begin, Lq, q0;
+  int k_begin, nk, c_begin, nc, nkv;
+};
+
+// Units are numbered ((b * Hq) + hq) * qunits + t, so consecutive units share
+// a sequence and head (their K/V stay hot in L2 while several CTAs read them).
+DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
+  Unit r;
+  const int per_b = a.Hq * a.qunits;
+  const int b = u / per_b;
+  const int rem = u - b * per_b;
+  r.hq = rem / a.qunits;
+  const int t = rem - r.hq * a.qunits;
+  r.hkv = r.hq / a.group;
+  r.q_begin = a.cu_q[b];
+  r.Lq = a.cu_q[b + 1] - r.q_begin;
+  r.q0 = t * kTileM;
+  r.valid = r.q0 < r.Lq;
+  r.k_begin = a.cu_k[b];
+  r.nk = a.cu_k[b + 1] - r.k_begin;
+  r.c_begin = 0;
+  r.nc = 0;
+  if (a.cu_c != nullptr) {
+    r.c_begin = a.cu_c[b];
+    r.nc = a.cu_c[b + 1] - r.c_begin;
+  }
+  r.nkv = (r.nc + kTileN - 1) / kTileN + (r.nk + kTileN - 1) / kTileN;
+  return r;
+}
+
+// Persistent kernel: CTA c processes units c, c + gridDim.x, ... Barrier
+// phases run on across units (ring counters below), so the producers load the
+// next unit's Q/K/V and the MMA warp starts its QKs while the softmax warps
+// still write the previous unit's output.
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
+                    const __grid_constant__ CUtensorMap tmVc, AttnKernelArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_base);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_units = args.total_units;
+
+  const uint32_t bar0 = base + kOffBar;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc + 16);
+
+#ifdef DLLM_TRACE
+  if (threadIdx.x < 16) g_trace_cnt[threadIdx.x] = 0;
+  if (threadIdx.x == 0) trace_err = args.err;
+#endif
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesQ; ++s) {
+      mbar_init(bar(BAR_QFULL + s), 1);
+      mbar_init(bar(BAR_QEMPTY + s), 1);
+    }
+    for (int s = 0; s < kStagesK; ++s) {
+      mbar_init(bar(BAR_KFULL + s), 1);
+      mbar_init(bar(BAR_KEMPTY + s), 1);
+    }
+    for (int s = 0; s < kStagesV; ++s) {
+      mbar_init(bar(BAR_VFULL + s), 1);
+      mbar_init(bar(BAR_VEMPTY + s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(BAR_SFULL + i), 1);
+      mbar_init(bar(BAR_PFULL + i), 8);  // one arrival per softmax warp
+    }
+    mbar_init(bar(BAR_OREADY), 1);
+    mbar_init(bar(BAR_OFULL), 1);
+    mbar_init(bar(BAR_XML), 128);  // every thread of warpgroup 1
+    mbar_init(bar(BAR_XF), 128);   // every thread of warpgroup 0
+    mbar_init(bar(BAR_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    if (args.cu_c != nullptr) {
+      tma_prefetch_desc(&tmKc);
+      tma_prefetch_desc(&tmVc);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 9 * 32) TRACE(1, 0, 0);
+
+  if (warp == 8 || warp == 10) {
+    // ------------------------------------------------------------------ TMA
+    // warp 8: Q tiles (2-deep ring) and the K ring; warp 10: the V ring (independent rings, so a wait
+    // for a free V stage never holds back a K load and vice versa). The whole
+    // warp walks the loop (uniformly); lane 0 issues the TMA copies and the
+    // barrier operations, all lanes help with paged cached tiles.
+    const bool kq = warp == 8;
+    const uint64_t pol_q = policy_evict_first();
+    const uint64_t pol_kv = policy_evict_last();
+    const int nst = kq ? kStagesK : kStagesV;
+    const int bfull = kq ? BAR_KFULL : BAR_VFULL;
+    const int bempty = kq ? BAR_KEMPTY : BAR_VEMPTY;
+    const uint32_t ring = base + (kq ? kOffK : kOffV);
+    const __nv_bfloat16* cache = kq ? args.kc : args.vc;
+    uint32_t q_it = 0;     // units whose Q was loaded (warp 8)
+    uint32_t done = 0;     // tiles issued into this ring
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      const Unit t = decode_unit(u, args);
+      if (!t.valid) continue;
+      if (kq) {
+        const int qs = q_it % kStagesQ;
+        if (q_it >= (uint32_t)kStagesQ)
+          ok = mbar_wait(bar(BAR_QEMPTY + qs), (q_it / kStagesQ - 1) & 1, abort_flag);
+        if (!ok) break;
+        if (lane == 0) {
+          const uint32_t dst = base + kOffQ + qs * kTileBytes;
+          const int row = t.q_begin + t.q0;
+          mbar_arrive_expect_tx(bar(BAR_QFULL + qs), kTileBytes);
+          tma_load_3d(dst, &tmQ, bar(BAR_QFULL + qs), 0, t.hq, row, pol_q);
+          tma_load_3d(dst + kChunkBytes, &tmQ, bar(BAR_QFULL + qs), 64, t.hq, row, pol_q);
+        }
+        ++q_it;
+      }
+      for (int j = 0; j < t.nkv; ++j) {
+        const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+        const int st = done % nst;
+        if (done >= (uint32_t)nst) ok = mbar_wait(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
+        if (!ok) break;
+        const uint32_t dk = ring + st * kTileBytes;
+        if (kt.seg == 0 && args.slots != nullptr) {
+          // Paged cached tile: rows slots[row0 .. row0+valid) of the cache.
+          // Consecutive slots (the page layout the model runner produces)
+          // become one TMA copy of the cache; anything else is gathered by
+          // the warp with bounds-checked 16-byte loads.
+          const int32_t* sp = args.slots + kt.row0;
+          const int s0 = sp[0];
+          int sl[4];
+          bool contig = s0 >= 0 && (int64_t)s0 + kt.valid <= args.num_slots;
+#pragma unroll
+          for (int r4 = 0; r4 < 4; ++r4) {
+            const int r = lane + 32 * r4;
+            sl[r4] = r < kt.valid ? sp[r] : -1;
+            if (r < kt.valid && sl[r4] != s0 + r) contig = false;
+          }
+          contig = __all_sync(0xffffffffu, contig);
+          if (contig) {
+            if (lane == 0) {
+              const CUtensorMap* mp = kq ? &tmKc : &tmVc;
+              mbar_arrive_expect_tx(bar(bfull + st), kTileBytes);
+              tma_load_3d(dk, mp, bar(bfull + st), 0, t.hkv, s0, pol_kv);
+              tma_load_3d(dk + kChunkBytes, mp, bar(bfull + st), 64, t.hkv, s0, pol_kv);
+            }
+          } else {
+            uint8_t* tile = smem + (dk - base);
+#pragma unroll 1
+            for (int r4 = 0; r4 < 4; ++r4) {
+              const int r = lane + 32 * r4;
+              const int64_t slot = sl[r4];
+              const bool in_range = slot >= 0 && slot < args.num_slots;
+              if (r < kt.valid && !in_range) set_error(args.err, kDevSlotOutOfRange);
+              const uint4* src = reinterpret_cast<const uint4*>(
+                  cache + (in_range ? slot : 0) * args.c_tok_stride + (int64_t)t.hkv * kD);
+#pragma unroll
+              for (int c16 = 0; c16 < 16; ++c16) {
+                uint4 val = make_uint4(0, 0, 0, 0);
+                if (r < kt.valid && in_range) val = __ldg(src + c16);
+                // SW128 layout: 16-byte unit index XOR (row mod 8) inside each 64-column half
+                const uint32_t off = (c16 >> 3) * kChunkBytes + r * 128 + (((c16 & 7) ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4*>(tile + off) = val;
+              }
+            }
+            fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(bfull + st));
+          }
+        } else if (lane == 0) {
+          const CUtensorMap* mp = kq ? (kt.seg == 0 ? &tmKc : &tmK) : (kt.seg == 0 ? &tmVc : &tmV);
+          mbar_arrive_expect_tx(bar(bfull + st), kTileBytes);
+          tma_load_3d(dk, mp, bar(bfull + st), 0, t.hkv, kt.row0, pol_kv);
+          tma_load_3d(dk + kChunkBytes, mp, bar(bfull + st), 64, t.hkv, kt.row0, pol_kv);
+        }
+        ++done;
+        if (lane == 0) TRACE(kq ? 2 : 3, j, 0);
+      }
+    }
+    if (lane == 0 && *abort_flag) {
+      // Drain: wait (bounded) for the loads that may still be in flight.
+      if (kq)
+        for (uint32_t n = (q_it > (uint32_t)kStagesQ ? q_it - kStagesQ : 0); n < q_it; ++n)
+          mbar_wait_drain(bar(BAR_QFULL + n % kStagesQ), (n / kStagesQ) & 1, 100000000ull);
+      for (uint32_t n = (done > (uint32_t)nst ? done - nst : 0); n < done; ++n)
+        mbar_wait_drain(bar(bfull + n % nst), (n / nst) & 1, 100000000ull);
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA
+    if (lane == 0) {
+      // Shared-memory descriptors are precomputed per buffer; a K-step adds a
+      // constant to the 14-bit start-address field (all offsets stay inside
+      // the 256 KB shared window, so the field never carries).
+      const uint32_t idesc_pv = make_idesc_bf16(128, 128, true);
+      const uint32_t idesc_qk_full = make_idesc_bf16(128, 128, false);
+      // Buffers of one kind are kTileBytes apart: stage n adds n * (kTileBytes >> 4).
+      const uint64_t dq0 = make_sw128_desc(base + kOffQ, 16, 1024);
+      const uint64_t dk0 = make_sw128_desc(base + kOffK, 16, 1024);
+      const uint64_t dv0 = make_sw128_desc(base + kOffV, kChunkBytes, 1024);
+      constexpr uint64_t kStageStep = kTileBytes >> 4;
+      // S(sb) = Q(qs) K(kst)^T over n_rows kv rows
+      auto qk = [&](int qs, int kst, int n_rows, uint32_t sb) {
+        const uint32_t idesc =
+            n_rows == kTileN ? idesc_qk_full : make_idesc_bf16(128, (n_rows + 15) & ~15, false);
+        const uint64_t a = dq0 + (uint64_t)qs * kStageStep, b = dk0 + (uint64_t)kst * kStageStep;
+        const uint32_t d = tmem + sb * 128;
+#pragma unroll
+        for (int s = 0; s < kD / 16; ++s) {
+          const uint64_t off = (uint64_t)(((s >> 2) * kChunkBytes + (s & 3) * 32) >> 4);
+          umma_ss(d, a + off, b + off, idesc, s > 0 ? 1u : 0u);
+        }
+      };
+      // O_h (+)= P_h V[64h .. 64h + 16 ksteps): P_h sits in TMEM at S buffer
+      // column 64h, V rows 64h.. are K-steps 4h.. of the stage.
+      auto pv_half = [&](int vst, uint32_t sb, int h, int ksteps, bool acc) {
+        const uint64_t b = dv0 + (uint64_t)vst * kStageStep;
+        const uint32_t d = tmem + 256 + h * 128;
+        const uint32_t a = tmem + sb * 128 + h * kHalfN;
+        if (ksteps == 4) {
+#pragma unroll
+          for (int s = 0; s < 4; ++s)
+            umma_ts(d, a + s * 8, b + (uint64_t)((4 * h + s) * (2048 >> 4)), idesc_pv,
+                    (acc || s > 0) ? 1u : 0u);
+        } else {
+          for (int s = 0; s < ksteps; ++s)
+            umma_ts(d, a + s * 8, b + (uint64_t)((4 * h + s) * (2048 >> 4)), idesc_pv,
+                    (acc || s > 0) ? 1u : 0u);
+        }
+      };
+      uint32_t q_it = 0, k_it = 0, v_it = 0;
+      uint32_t g = 0;  // KV tiles whose PVs were issued (all units), = S tile index
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        const Unit t = decode_unit(u, args);
+        if (!t.valid) continue;
+        const int qs = q_it % kStagesQ;
+        ok = mbar_wait(bar(BAR_QFULL + qs), (q_it / kStagesQ) & 1, abort_flag);
+        if (!ok) break;
+        ++q_it;
+        if (t.nkv == 0) {
+          umma_commit(bar(BAR_QEMPTY + qs));
+          continue;
+        }
+        // Prologue: S of the unit's first two tiles.
+        const int npro = t.nkv < 2 ? t.nkv : 2;
+        for (int j = 0; j < npro && ok; ++j) {
+          const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+          const int kst = k_it % kStagesK;
+          ok = mbar_wait(bar(BAR_KFULL + kst), (k_it / kStagesK) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          qk(qs, kst, kt.valid, (g + j) & 1);
+          umma_commit(bar(BAR_SFULL + ((g + j) & 1)));
+          umma_commit(bar(BAR_KEMPTY + kst));
+          ++k_it;
+        }
+        if (!ok) break;
+        if (t.nkv <= 2) umma_commit(bar(BAR_QEMPTY + qs));  // every QK of the unit issued
+        bool b_started = false;  // O_b written in this unit
+        for (int j = 0; j < t.nkv && ok; ++j, ++g) {
+          const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+          const uint32_t sb = g & 1;
+          const int vst = v_it % kStagesV;
+          ok = mbar_wait(bar(BAR_VFULL + vst), (v_it / kStagesV) & 1, abort_flag);
+          if (!ok) break;
+          ok = mbar_wait(bar(BAR_PFULL + sb), (g >> 1) & 1, abort_flag);
+          if (!ok) break;
+          TRACE(6, j, 0);
+          tc_fence_after();
+          const int ks = (kt.valid + 15) >> 4;  // 1..8 K-steps
+          pv_half(vst, sb, 0, ks < 4 ? ks : 4, j > 0);
+          if (ks > 4) {
+            pv_half(vst, sb, 1, ks - 4, b_started);
+            b_started = true;
+          }
+          umma_commit(bar(BAR_VEMPTY + vst));
+          umma_commit(bar(BAR_OREADY));
+          ++v_it;
+          if (j + 2 < t.nkv) {
+            const KvTile kn = kv_tile(j + 2, t.nc, t.c_begin, t.nk, t.k_begin);
+            const int kst = k_it % kStagesK;
+            ok = mbar_wait(bar(BAR_KFULL + kst), (k_it / kStagesK) & 1, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            qk(qs, kst, kn.valid, sb);  // tile g + 2 uses the same S buffer
+            umma_commit(bar(BAR_SFULL + sb));
+            umma_commit(bar(BAR_KEMPTY + kst));
+            ++k_it;
+            if (j + 3 == t.nkv) umma_commit(bar(BAR_QEMPTY + qs));  // last QK issued
+          }
+          TRACE(7, j, 0);
+        }
+        if (!ok) break;
+        umma_commit(bar(BAR_OFULL));
+      }
+      // Make sure every issued MMA has finished before TMEM is released.
+      umma_commit(bar(BAR_DRAIN));
+      mbar_wait_drain(bar(BAR_DRAIN), 0, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int wg = warp >> 2;           // 0: kv rows 0-63 of a tile, 1: rows 64-127
+    const int wq = warp & 3;            // warp within the warpgroup
+    const int row_in_tile = threadIdx.x & 127;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t tOwn = tmem + lane_base + 256 + wg * 128;  // this warpgroup's accumulator
+    const uint32_t tOa = tmem + lane_base + 256;
+    const uint32_t tOb = tmem + lane_base + 384;
+    float2* xch = reinterpret_cast<float2*>(smem + kOffXch);
+    const float sl2 = args.scale_log2;
+    uint32_t g = 0, o_it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      const Unit t = decode_unit(u, args);
+      if (!t.valid) continue;
+      float m = -INFINITY;  // running max (log2 units), -inf until a valid column
+      float l = 0.f;
+      for (int j = 0; j < t.nkv; ++j, ++g) {
+        const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+        const uint32_t sb = g & 1;
+        ok = mbar_wait(bar(BAR_SFULL + sb), (g >> 1) & 1, abort_flag);
+        if (!ok) break;
+        if (row_in_tile == 0) TRACE(10, j, wg);
+        tc_fence_after();
+        const uint32_t tS = tmem + lane_base + sb * 128 + wg * kHalfN;
+        int nv = kt.valid - wg * kHalfN;  // valid columns of this half (warp-uniform)
+        nv = nv < 0 ? 0 : (nv > kHalfN ? kHalfN : nv);
+        if (nv > 0) {
+          uint32_t s[2][32];
+          tmem_ld32(tS, s[0]);
+          tmem_ld32(tS + 32, s[1]);
+          tmem_wait_ld();
+          if (nv < kHalfN) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (c * 32 + e >= nv) s[c][e] = __float_as_uint(-INFINITY);
+          }
+          // row max: two independent 3-input max chains
+          float mq[2];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float a = __uint_as_float(s[c][0]);
+#pragma unroll
+            for (int e = 1; e < 31; e += 2)
+              a = max3f(a, __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]));
+            mq[c] = fmaxf(a, __uint_as_float(s[c][31]));
+          }
+          const float mxs = fmaxf(mq[0], mq[1]) * sl2;
+          if (m == -INFINITY) {
+            m = mxs;  // first valid columns: the accumulator starts fresh
+          } else {
+            // Lazy rescaling: keep a stale maximum while the new one exceeds
+            // it by at most 8 (log2 units), so P stays <= 256 and O/l stay
+            // exact up to rounding; rescale O only when a warp needs it.
+            const bool need = mxs > m + 8.f;
+            if (__any_sync(0xffffffffu, need)) {
+              const float mn = fmaxf(m, mxs);
+              const float alpha = ex2_approx(m - mn);
+              m = mn;
+              l *= alpha;
+              // The accumulator must hold every PV up to tile g-1: PV(g-2)
+              // completed before S(g) did, so one more completion of OREADY
+              // (parity of tile g-1) is all there is to wait for.
+              ok = mbar_wait(bar(BAR_OREADY), (g - 1) & 1, abort_flag);
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tmem_ld32(tOwn + c * 32, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                tmem_st32(tOwn + c * 32, o);
+              }
+            }
+          }
+          float rs;
+          if (nv < kHalfN) {
+            rs = exp_store_half<0>(s, sl2, m, tS);  // masked columns: MUFU only (exact 0)
+          } else {
+            rs = exp_store_half<kSmPoly>(s, sl2, m, tS);
+          }
+          l += rs;
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(BAR_PFULL + sb));
+        if (row_in_tile == 0) TRACE(13, j, wg);
+      }
+      if (!ok) break;
+      // Epilogue: merge the two halves, O / l -> bf16 -> global. Warpgroup w
+      // writes output columns [64w, 64w + 64).
+      const int row = t.q0 + row_in_tile;
+      const bool row_ok = row < t.Lq;
+      __nv_bfloat16* orow = args.o + (int64_t)(t.q_begin + row) * args.o_tok_stride +
+                            (int64_t)t.hq * args.o_head_stride + wg * kHalfN;
+      if (t.nkv > 0) {
+        ok = mbar_wait(bar(BAR_OFULL), o_it & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        // Merge factors: O = ca * O_a + cb * O_b with ca = 2^(m0-m)/L,
+        // cb = 2^(m1-m)/L, m = max(m0, m1), L = l0 2^(m0-m) + l1 2^(m1-m).
+        // Warpgroup 0 always has a valid column (every tile has >= 1 row);
+        // warpgroup 1 may have none (m1 = -inf), then O_b was never written.
+        float ca, cb;
+        if (wg == 1) {
+          xch[row_in_tile] = make_float2(m, l);
+          mbar_arrive(bar(BAR_XML));
+          ok = mbar_wait(bar(BAR_XF), o_it & 1, abort_flag);
+          if (!ok) break;
+          const float2 f = xch[row_in_tile];
+          ca = f.x;
+          cb = f.y;
+        } else {
+          ok = mbar_wait(bar(BAR_XML), o_it & 1, abort_flag);
+          if (!ok) break;
+          const float2 o1 = xch[row_in_tile];
+          const float mm = fmaxf(m, o1.x);
+          const float fa = ex2_approx(m - mm);
+          const float fb = o1.x == -INFINITY ? 0.f : ex2_approx(o1.x - mm);
+          const float inv = 1.f / (l * fa + o1.y * fb);
+          ca = fa * inv;
+          cb = fb * inv;
+          xch[row_in_tile] = make_float2(ca, cb);
+          mbar_arrive(bar(BAR_XF));
+        }
+        ++o_it;
+        if (row_in_tile == 0) TRACE(14, 0, wg);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t oa[32], ob[32];
+          tmem_ld32(tOa + wg * kHalfN + c * 32, oa);
+          tmem_ld32(tOb + wg * kHalfN + c * 32, ob);
+          tmem_wait_ld();
+          if (row_ok) {
+            float v[32];
+            if (cb != 0.f) {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                v[e] = fmaf(__uint_as_float(oa[e]), ca, __uint_as_float(ob[e]) * cb);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(oa[e]) * ca;
+            }
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w4;
+              w4.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+              w4.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+              w4.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+              w4.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+              dst[q] = w4;
+            }
+          }
+        }
+        // O is read out; the next unit's first PV may overwrite it once every
+        // softmax warp arrives on its first P barrier (program order + fence).
+        tc_fence_before();
+      } else if (row_ok) {
+        // No keys at all: the output row is zero.
+        uint4* dst = reinterpret_cast<uint4*>(orow);
+        for (int v = 0; v < kHalfN / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+
+  if (warp < 8 && row_in_tile_of(threadIdx.x) == 0) TRACE(15, 0, warp >> 2);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && *abort_flag) set_error(args.err, kDevWaitTimeout);
+}
+
+}  // namespace split
+
+cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                            const CUtensorMap& tmKc, const CUtensorMap& tmVc,
+                            const AttnKernelArgs& args, int max_q, int num_sms,
+                            cudaStream_t stream) {
+  // The smem opt-in is per device; remember it for up to 64 devices.
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(split::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)split::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  AttnKernelArgs a = args;
+  a.qunits = (max_q + split::kTileM - 1) / split::kTileM;
+  const long long units = (long long)a.B * a.Hq * a.qunits;
+  if (units == 0) return cudaSuccess;
+  if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
+  a.total_units = (int)units;
+  const int grid = (int)(units < num_sms ? units : num_sms);
+  split::attn_fwd_kernel<<<grid, split::kThreads, split::kSmemBytes, stream>>>(tmQ, tmK, tmV, tmKc, tmVc, a);
+  return cudaGetLastError();
+}
+
+}  // namespace dllm

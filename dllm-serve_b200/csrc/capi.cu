@@ -158,10 +158,17 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.kc = reinterpret_cast<const __nv_bfloat16*>(kc);
   a.vc = reinterpret_cast<const __nv_bfloat16*>(vc);
   a.c_tok_stride = kc_tok_stride;
-  a.qpairs = 0;
+  a.qunits = 0;
   a.total_units = 0;
-  cudaError_t e = dllm::launch_attn_fwd(tq, tk, tv, tkc, tvc, a, max_q, num_sms_of_current_device(),
-                                        reinterpret_cast<cudaStream_t>(stream));
+  // Query segments that fit one tile (the reuse steps' fresh blocks) go to the
+  // split kernel, which keeps both softmax warpgroups busy on a lone tile.
+  const int sms = num_sms_of_current_device();
+  cudaError_t e =
+      max_q <= dllm::kSplitMaxQ
+          ? dllm::launch_attn_fwd_split(tq, tk, tv, tkc, tvc, a, max_q, sms,
+                                        reinterpret_cast<cudaStream_t>(stream))
+          : dllm::launch_attn_fwd(tq, tk, tv, tkc, tvc, a, max_q, sms,
+                                  reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
   return DLLM_OK;
 }

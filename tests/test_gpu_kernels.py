@@ -234,6 +234,44 @@ def test_attention_cached_segments(dev, hq, hkv):
     _status_clear(dev)
 
 
+SPLIT_EDGE = [  # (query rows, cached rows, fresh key rows) per sequence, all query segments <= 128
+    [(32, 40, 32), (1, 0, 1), (17, 1, 17), (64, 63, 64)],
+    [(65, 64, 65), (128, 65, 128), (100, 129, 100), (32, 300, 32)],
+    [(128, 0, 128), (5, 0, 64), (6, 0, 65), (7, 127, 1)],
+]
+
+
+@pytest.mark.parametrize("case", range(len(SPLIT_EDGE)), ids=[f"e{i}" for i in range(len(SPLIT_EDGE))])
+@pytest.mark.parametrize("hq,hkv", [(4, 4), (7, 1)])
+def test_attention_single_tile_segments(dev, case, hq, hkv):
+    """Launches whose query segments fit one 128-row tile (the split kernel): key
+    tiles whose second half has no valid rows (cached segments of 40/63/64 rows,
+    1-64 fresh rows), a second half that stays empty for a whole sequence, and
+    partial tiles at the end of the cached segment."""
+    seqs = SPLIT_EDGE[case]
+    lq = [s[0] for s in seqs]
+    lc = [s[1] for s in seqs]
+    lk = [s[2] for s in seqs]
+    g = I.gen(120 + case * 7 + hq)
+    D = 128
+    q = I.normal(g, (sum(lq), hq, D))
+    k, v = I.normal(g, (sum(lk), hkv, D)), I.normal(g, (sum(lk), hkv, D))
+    kc, vc = I.normal(g, (sum(lc), hkv, D)), I.normal(g, (sum(lc), hkv, D))
+    ref = R.varlen_attention(q, k, v, _cu(lq), _cu(lk), D ** -0.5, kc, vc, _cu(lc))
+    t = lambda x: x.to(dev, torch.bfloat16)
+    i32 = lambda x: torch.tensor(_cu(x), dtype=torch.int32, device=dev)
+    out = torch.full((sum(lq), hq, D), float("nan"), dtype=torch.bfloat16, device=dev)
+    _ops().varlen_attention(t(q), t(k), t(v), i32(lq), i32(lk), max(lq), D ** -0.5,
+                            k_cached=t(kc), v_cached=t(vc), cu_seqlens_c=i32(lc), out=out)
+    torch.cuda.synchronize()
+    _check_attn(out, ref, f"case {case} hq={hq} hkv={hkv}")
+    # the same keys without a cached segment
+    ref2 = R.varlen_attention(q, k, v, _cu(lq), _cu(lk), D ** -0.5)
+    out2 = _ops().varlen_attention(t(q), t(k), t(v), i32(lq), i32(lk), max(lq), D ** -0.5)
+    _check_attn(out2, ref2, f"case {case} fresh only")
+    _status_clear(dev)
+
+
 def test_attention_c2_full_size_sampled(dev):
     """Config-2 shapes (B=16, L in [384,1152], 32 MHA heads): every output
     row finite; a sample of (sequence, head) pairs checked against the oracle."""
