@@ -351,7 +351,9 @@ def run_ours(args, lens):
     roof = {"kernel": "dllm::attn_fwd_kernel", "bound": "tensor", "achieved": achieved,
             "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_kind": f"{peak_kind} bf16 dense (sustained)",
-            "traffic": profile_traffic("attn_fwd_c2"),
+            # ncu capture of a full 32-head layer; a rank's launch covers Hq/world heads
+            "traffic": (None if profile_traffic("attn_fwd_c2") is None
+                        else profile_traffic("attn_fwd_c2") * Hq / HEADS),
             "algorithmic_per_launch": f"{flops_step_local / LAYERS / 1e9:.1f} GFLOP (4*sum(L^2)*Hq*D)",
             "mean_launch_ms": mean_launch_ms}
 
