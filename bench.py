@@ -729,7 +729,7 @@ def run_sparse_cycle(args):
 def run_kernels_case(args):
     """Small profiling case: each native kernel launched 3 times on inputs
     larger than L2 (one c2 layer for attention and the KV store, config-5
-    shapes for scoring/top-k, config-3 reuse shapes for cached attention)."""
+    shapes for scoring/top-k and for the reuse-state attention)."""
     from dllmserve_b200 import _native, ops
 
     _native.lib()
@@ -763,14 +763,19 @@ def run_kernels_case(args):
     for _ in range(3):
         ops.select_kv_store(q5, k5, v5, desc, L5 - blk, True, kc5, vc5, slots5)
     del q5, k5, v5
-    # config 3 reuse state: B=8, 32 block queries, 304 cached + 32 fresh keys
-    B3, n3 = 8, 304
+    # config 5 reuse state (split kernel, paged cache): B=8, 32 block queries,
+    # 1,144 cached rows (runs of whole pages, as the block manager allocates) + 32 fresh keys
+    B3, n3 = 8, n_keep
     q3, k3, v3 = rnd(B3 * 32, HEADS, HEAD_DIM), rnd(B3 * 32, KV_HEADS, HEAD_DIM), rnd(B3 * 32, KV_HEADS, HEAD_DIM)
-    kc3, vc3 = rnd(B3 * n3, KV_HEADS, HEAD_DIM), rnd(B3 * n3, KV_HEADS, HEAD_DIM)
     cq = torch.arange(0, B3 * 32 + 1, 32, dtype=torch.int32, device=dev)
     cc = torch.arange(0, B3 * n3 + 1, n3, dtype=torch.int32, device=dev)
+    ppseq = (n3 + 255) // 256
+    page_order = torch.randperm(pages5, device=dev, generator=g)[:B3 * ppseq]
+    slot3 = torch.cat([torch.cat([torch.arange(256, device=dev) + 256 * int(p) for p in page_order[b * ppseq:(b + 1) * ppseq]])[:n3]
+                       for b in range(B3)]).to(torch.int32)
     for _ in range(3):
-        ops.varlen_attention(q3, k3, v3, cq, cq, 32, k_cached=kc3, v_cached=vc3, cu_seqlens_c=cc)
+        ops.varlen_attention(q3, k3, v3, cq, cq, 32, k_cache=kc5, v_cache=vc5, slots=slot3,
+                             cu_seqlens_slots=cc)
     torch.cuda.synchronize()
     if ops.read_device_status(dev) != 0:
         raise RuntimeError("a kernel reported a device error")

@@ -8,9 +8,12 @@
 //
 // One CTA per (sequence, KV head) with head_select, one CTA per sequence
 // otherwise. The pass over the candidate keys is HBM-bound (one read of each
-// candidate row); ranking runs in shared memory as a bitonic sort of 64-bit
-// keys  (order-preserving score bits << 32) | (0xffffffff - candidate)  so the
-// result is "descending score, ties by ascending candidate index".
+// candidate row, several rows in flight per half warp). Ranking runs in shared
+// memory: a radix select (4 passes of 8 bits) finds the n_keep-th largest
+// pooled score T, the keys above T plus the lowest-index keys equal to T are
+// compacted, and only those n_keep keys are bitonic-sorted as 64-bit
+// (order-preserving score bits << 32) | (0xffffffff - candidate), so the result
+// is "descending score, ties by ascending candidate index".
 #include "common.cuh"
 #include "select_kv.h"
 
@@ -21,6 +24,8 @@ namespace {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kD = 128;
+constexpr int kRowsInFlight = 4;                     // candidate rows per half warp per pass
+constexpr int kFullSortMax = 2048;  // up to this many (padded) keys a full sort beats radix select
 
 DLLM_DEVICE uint32_t order_bits(float f) {
   uint32_t u = __float_as_uint(f);
@@ -32,6 +37,17 @@ DLLM_DEVICE void bf16x4_to_f32(uint2 w, float (&x)[4]) {
   x[1] = __uint_as_float(w.x & 0xffff0000u);
   x[2] = __uint_as_float(w.y << 16);
   x[3] = __uint_as_float(w.y & 0xffff0000u);
+}
+
+DLLM_DEVICE void bf16x8_to_f32(uint4 w, float (&x)[8]) {
+  x[0] = __uint_as_float(w.x << 16);
+  x[1] = __uint_as_float(w.x & 0xffff0000u);
+  x[2] = __uint_as_float(w.y << 16);
+  x[3] = __uint_as_float(w.y & 0xffff0000u);
+  x[4] = __uint_as_float(w.z << 16);
+  x[5] = __uint_as_float(w.z & 0xffff0000u);
+  x[6] = __uint_as_float(w.w << 16);
+  x[7] = __uint_as_float(w.w & 0xffff0000u);
 }
 
 DLLM_DEVICE float warp_sum(float v) {
@@ -46,7 +62,7 @@ DLLM_DEVICE int cand_token(int c, int blk_start, int blk_len) {
 }
 
 template <bool kHeadSelect>
-__global__ void __launch_bounds__(kThreads, 1) select_kv_kernel(SelectArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int seq = blockIdx.y;
   const int h = blockIdx.x;  // KV head (head_select) or 0
@@ -63,14 +79,18 @@ __global__ void __launch_bounds__(kThreads, 1) select_kv_kernel(SelectArgs a) {
     return;
   }
 
-  // shared memory: q_avg [nq][128] f32 | scores [max_klen] f32 | keys [p2] u64
+  // shared memory: q_avg [nq][128] f32 | scores [max_klen] f32 | sel [p2(max_klen)] u64 |
+  // hist [256] u32 | wsum [kWarps] u32 | misc [4] u32
   const int nq = kHeadSelect ? a.group : a.Hq;  // query heads that score this CTA's rows
   float* q_avg = reinterpret_cast<float*>(smem);
   float* scores = q_avg + nq * kD;
-  uint64_t* keys = reinterpret_cast<uint64_t*>(
+  int p2max = 1;
+  while (p2max < a.max_klen) p2max <<= 1;
+  uint64_t* sel = reinterpret_cast<uint64_t*>(
       smem + (((size_t)nq * kD * 4 + (size_t)a.max_klen * 4 + 15) & ~(size_t)15));
-  int p2 = 1;
-  while (p2 < Klen) p2 <<= 1;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(sel + p2max);
+  uint32_t* wsum = hist + 256;
+  uint32_t* misc = wsum + kWarps;
 
   // 1) q_avg = mean over the block's query rows (fp32), attention.py:367 / :315.
   const int qh0 = kHeadSelect ? h * a.group : 0;
@@ -78,51 +98,95 @@ __global__ void __launch_bounds__(kThreads, 1) select_kv_kernel(SelectArgs a) {
     const int g = e / kD, dd = e % kD;
     const __nv_bfloat16* qp =
         a.q + (int64_t)(tok_start + blk_start) * a.q_tok_stride + (int64_t)(qh0 + g) * kD + dd;
-    float s = 0.f;
-    for (int t = 0; t < blk_len; ++t) s += __bfloat162float(qp[(int64_t)t * a.q_tok_stride]);
+    // 8 independent partial sums keep 8 loads in flight per thread
+    float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int t = 0;
+    for (; t + 8 <= blk_len; t += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s8[u] += __bfloat162float(qp[(int64_t)(t + u) * a.q_tok_stride]);
+    }
+    for (; t < blk_len; ++t) s8[0] += __bfloat162float(qp[(int64_t)t * a.q_tok_stride]);
+    const float s = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
     q_avg[e] = s / (float)blk_len;
   }
+  if (threadIdx.x == 0) misc[2] = 0;  // selection counter
   __syncthreads();
 
-  // 2) scores (one warp per candidate row), attention.py:374-384 / :317-326.
+  // 2) scores, attention.py:374-384 / :317-326.
   if (kHeadSelect) {
+    // Half warp per candidate row (16 lanes x 8 bf16 = the 128-dim head row),
+    // kRowsInFlight rows per half warp per pass.
     const int G = a.group;
-    for (int c = warp; c < Klen; c += kWarps) {
-      const int tok = tok_start + cand_token(c, blk_start, blk_len);
-      const uint2 w = __ldg(reinterpret_cast<const uint2*>(a.k + (int64_t)tok * a.k_tok_stride +
-                                                           (int64_t)h * kD) + lane);
-      float x[4];
-      bf16x4_to_f32(w, x);
-      float best = -INFINITY;
-      for (int g = 0; g < G; ++g) {
-        const float4 qa = reinterpret_cast<const float4*>(q_avg + g * kD)[lane];
-        float p = qa.x * x[0];
-        p = fmaf(qa.y, x[1], p);
-        p = fmaf(qa.z, x[2], p);
-        p = fmaf(qa.w, x[3], p);
-        p = warp_sum(p);
-        best = fmaxf(best, p);
+    const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
+    constexpr int kHalves = kThreads / 16;
+    // The trip count is uniform over the warp (both halves step together), so
+    // the 16-lane shuffle reductions always run with all 32 lanes.
+    for (int cw = 2 * warp; cw < Klen; cw += kHalves * kRowsInFlight) {
+      const int c0 = cw + (hw & 1);
+      uint4 w[kRowsInFlight];
+#pragma unroll
+      for (int r = 0; r < kRowsInFlight; ++r) {
+        const int c = c0 + r * kHalves;
+        w[r] = make_uint4(0, 0, 0, 0);
+        if (c < Klen) {
+          const int tok = tok_start + cand_token(c, blk_start, blk_len);
+          w[r] = __ldg(reinterpret_cast<const uint4*>(a.k + (int64_t)tok * a.k_tok_stride +
+                                                      (int64_t)h * kD) + hl);
+        }
       }
-      if (lane == 0) scores[c] = __fdiv_rn(best, a.sqrt_d);
+#pragma unroll
+      for (int r = 0; r < kRowsInFlight; ++r) {
+        float x[8];
+        bf16x8_to_f32(w[r], x);
+        float best = -INFINITY;
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl];
+          const float4 qb = reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl + 1];
+          float p = qa.x * x[0];
+          p = fmaf(qa.y, x[1], p);
+          p = fmaf(qa.z, x[2], p);
+          p = fmaf(qa.w, x[3], p);
+          p = fmaf(qb.x, x[4], p);
+          p = fmaf(qb.y, x[5], p);
+          p = fmaf(qb.z, x[6], p);
+          p = fmaf(qb.w, x[7], p);
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+          best = fmaxf(best, p);
+        }
+        const int c = c0 + r * kHalves;
+        if (hl == 0 && c < Klen) scores[c] = __fdiv_rn(best, a.sqrt_d);
+      }
     }
   } else {
     // Shared ranking: sum over every query head h of q_avg[h] . k[c, h / group].
+    // Warp per candidate row, 16 bytes per lane, kVecBatch loads in flight per lane.
     const int Hkv = a.Hkv, G = a.group;
-    const int row_vec = Hkv * kD / 4;  // uint2 (4 bf16) per lane step
+    const int row_vec = Hkv * kD / 8;  // uint4 (8 bf16) per lane step
+    constexpr int kVecBatch = 8;
     for (int c = warp; c < Klen; c += kWarps) {
       const int tok = tok_start + cand_token(c, blk_start, blk_len);
-      const uint2* kr = reinterpret_cast<const uint2*>(a.k + (int64_t)tok * a.k_tok_stride);
+      const uint4* kr = reinterpret_cast<const uint4*>(a.k + (int64_t)tok * a.k_tok_stride);
       float p = 0.f;
-      for (int e = lane; e < row_vec; e += 32) {
-        float x[4];
-        bf16x4_to_f32(__ldg(kr + e), x);
-        const int hk = (e * 4) / kD, dd = (e * 4) % kD;
-        for (int g = 0; g < G; ++g) {
-          const float* qa = q_avg + (hk * G + g) * kD + dd;
-          p = fmaf(qa[0], x[0], p);
-          p = fmaf(qa[1], x[1], p);
-          p = fmaf(qa[2], x[2], p);
-          p = fmaf(qa[3], x[3], p);
+      for (int e0 = 0; e0 < row_vec; e0 += 32 * kVecBatch) {
+        uint4 w[kVecBatch];
+#pragma unroll
+        for (int u = 0; u < kVecBatch; ++u) {
+          const int e = e0 + u * 32 + lane;
+          w[u] = e < row_vec ? __ldg(kr + e) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kVecBatch; ++u) {
+          const int e = e0 + u * 32 + lane;
+          if (e >= row_vec) continue;
+          float x[8];
+          bf16x8_to_f32(w[u], x);
+          const int hk = (e * 8) / kD, dd = (e * 8) % kD;
+          for (int g = 0; g < G; ++g) {
+            const float* qa = q_avg + (hk * G + g) * kD + dd;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) p = fmaf(qa[i], x[i], p);
+          }
         }
       }
       p = warp_sum(p);
@@ -131,35 +195,122 @@ __global__ void __launch_bounds__(kThreads, 1) select_kv_kernel(SelectArgs a) {
   }
   __syncthreads();
 
-  // 3) max_pool1d(kernel=pool_k, stride 1, padding pool_k/2)[:Klen] + sort keys,
-  //    attention.py:386-393 / :328-335.
+  // 3) max_pool1d(kernel=pool_k, stride 1, padding pool_k/2)[:Klen]
+  //    (attention.py:386-393 / :328-335), evaluated where it is read, as
+  //    order-preserving bits.
   const int pad = pool_k / 2;
-  for (int c = threadIdx.x; c < p2; c += kThreads) {
-    uint64_t key = 0;  // padding sorts last
-    if (c < Klen) {
-      float m = scores[c];
-      if (pool_k > 1) {
-        const int lo = max(0, c - pad), hi = min(Klen - 1, c - pad + pool_k - 1);
-        m = -INFINITY;
-        for (int j = lo; j <= hi; ++j) m = fmaxf(m, scores[j]);
-      }
-      key = ((uint64_t)order_bits(m) << 32) | (uint64_t)(0xffffffffu - (uint32_t)c);
+  auto pooled = [&](int c) -> uint32_t {
+    float m = scores[c];
+    if (pool_k > 1) {
+      const int lo = max(0, c - pad), hi = min(Klen - 1, c - pad + pool_k - 1);
+      m = -INFINITY;
+      for (int j = lo; j <= hi; ++j) m = fmaxf(m, scores[j]);
     }
-    keys[c] = key;
+    return order_bits(m);
+  };
+
+  int p2k = 1;
+  while (p2k < Klen) p2k <<= 1;
+  const bool full_sort = p2k <= kFullSortMax;
+  // 4) radix select (MSB first, 8 bits a pass) of the n_keep-th largest pooled
+  //    score T; `krem` = how many keys equal to T belong to the top n_keep.
+  //    Small candidate sets skip it (T = 0, every key selected, full sort).
+  uint32_t prefix = 0, mask = 0;
+  int krem = full_sort ? Klen : n_keep;
+  for (int shift = 24; shift >= 0 && !full_sort; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
+    __syncthreads();
+    for (int cb = warp * 32; cb < Klen; cb += kThreads) {  // warp-uniform trip count
+      const int c = cb + lane;
+      const uint32_t v = c < Klen ? pooled(c) : 0u;
+      const bool match = c < Klen && (v & mask) == prefix;
+      const uint32_t active = __ballot_sync(0xffffffffu, match);
+      if (match) {
+        const uint32_t dig = (v >> shift) & 255u;
+        const uint32_t peers = __match_any_sync(active, dig);
+        if (lane == __ffs(peers) - 1) atomicAdd(&hist[dig], (uint32_t)__popc(peers));
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l holds bins 255-8l .. 248-8l (descending digit order)
+      uint32_t cnt[8], sum = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        cnt[i] = hist[255 - 8 * lane - i];
+        sum += cnt[i];
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      const uint32_t excl = incl - sum;
+      if (excl < (uint32_t)krem && (uint32_t)krem <= incl) {
+        uint32_t acc = excl;
+        for (int i = 0; i < 8; ++i) {
+          if (acc + cnt[i] >= (uint32_t)krem) {
+            misc[0] = 255u - 8u * lane - i;
+            misc[1] = (uint32_t)krem - acc;
+            break;
+          }
+          acc += cnt[i];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= misc[0] << shift;
+    mask |= 255u << shift;
+    krem = (int)misc[1];
   }
+  const uint32_t T = prefix;  // order bits are never 0 (NaN-free scores), so T = 0 keeps every key
+
+  // 5) compaction: every key above T, and the krem keys equal to T with the
+  //    lowest candidate indices (ties by ascending index), in any order.
+  {
+    uint32_t eq_base = 0;
+    const uint32_t lt_mask = (1u << lane) - 1u;
+    for (int c0 = 0; c0 < Klen; c0 += kThreads) {
+      const int c = c0 + threadIdx.x;
+      const uint32_t v = c < Klen ? pooled(c) : 0u;
+      const bool gt = c < Klen && v > T;
+      const bool eq = c < Klen && v == T;
+      const uint32_t be = __ballot_sync(0xffffffffu, eq);
+      if (lane == 0) wsum[warp] = (uint32_t)__popc(be);
+      __syncthreads();
+      uint32_t before = 0, total = 0;
+      for (int w = 0; w < kWarps; ++w) {
+        const uint32_t x = wsum[w];
+        before += w < warp ? x : 0u;
+        total += x;
+      }
+      const uint32_t rank = eq_base + before + (uint32_t)__popc(be & lt_mask);
+      if (gt || (eq && rank < (uint32_t)krem)) {
+        const uint32_t pos = atomicAdd(&misc[2], 1u);
+        sel[pos] = ((uint64_t)v << 32) | (uint64_t)(0xffffffffu - (uint32_t)c);
+      }
+      eq_base += total;
+      __syncthreads();
+    }
+  }
+  const int n_sel = full_sort ? Klen : n_keep;
+  int p2 = 1;
+  while (p2 < n_sel) p2 <<= 1;
+  for (int i = n_sel + threadIdx.x; i < p2; i += kThreads) sel[i] = 0;  // padding sorts last
   __syncthreads();
 
-  // 4) descending bitonic sort of p2 keys, attention.py:402-404 / :341.
+  // 6) descending bitonic sort of the n_keep selected keys, attention.py:402-404 / :341.
   for (int k = 2; k <= p2; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = threadIdx.x; i < p2; i += kThreads) {
         const int ixj = i ^ j;
         if (ixj > i) {
-          const uint64_t x = keys[i], y = keys[ixj];
+          const uint64_t x = sel[i], y = sel[ixj];
           const bool desc = (i & k) == 0;
           if (desc ? (x < y) : (x > y)) {
-            keys[i] = y;
-            keys[ixj] = x;
+            sel[i] = y;
+            sel[ixj] = x;
           }
         }
       }
@@ -167,35 +318,47 @@ __global__ void __launch_bounds__(kThreads, 1) select_kv_kernel(SelectArgs a) {
     }
   }
 
-  // 5) indices out + gather/store of the selected rows (attention.py:405-411, :222-233).
+  // 7) indices out + gather/store of the selected rows (attention.py:405-411, :222-233).
   for (int j = threadIdx.x; j < n_keep && a.top_idx != nullptr; j += kThreads) {
-    const int c = (int)(0xffffffffu - (uint32_t)(keys[j] & 0xffffffffu));
+    const int c = (int)(0xffffffffu - (uint32_t)(sel[j] & 0xffffffffu));
     const int64_t o = kHeadSelect ? (int64_t)idx_off + (int64_t)h * n_keep + j : (int64_t)idx_off + j;
     a.top_idx[o] = c;
   }
   if (kHeadSelect) {
-    // 16 lanes x 16 B = one 256-byte head row per half warp.
+    // 16 lanes x 16 B = one 256-byte head row per half warp, kRowsInFlight rows at a time.
     const int half = threadIdx.x >> 4, hl = threadIdx.x & 15;
-    for (int j = half; j < n_keep; j += kThreads / 16) {
-      const int c = (int)(0xffffffffu - (uint32_t)(keys[j] & 0xffffffffu));
-      const int64_t slot = a.slots[slot_off + j];
-      if (slot < 0) continue;
-      if (slot >= a.num_slots) {
-        if (hl == 0) set_error(a.err, kDevSlotOutOfRange);
-        continue;
+    constexpr int kHalves = kThreads / 16;
+    for (int j0 = half; j0 < n_keep; j0 += kHalves * kRowsInFlight) {
+      uint4 kv[kRowsInFlight][2];
+      int64_t dst[kRowsInFlight];
+#pragma unroll
+      for (int r = 0; r < kRowsInFlight; ++r) {
+        const int j = j0 + r * kHalves;
+        dst[r] = -1;
+        if (j < n_keep) {
+          const int c = (int)(0xffffffffu - (uint32_t)(sel[j] & 0xffffffffu));
+          const int64_t slot = a.slots[slot_off + j];
+          if (slot >= a.num_slots) {
+            if (hl == 0) set_error(a.err, kDevSlotOutOfRange);
+          } else if (slot >= 0) {
+            const int64_t tok = tok_start + cand_token(c, blk_start, blk_len);
+            kv[r][0] = __ldg(reinterpret_cast<const uint4*>(a.k + tok * a.k_tok_stride + (int64_t)h * kD) + hl);
+            kv[r][1] = __ldg(reinterpret_cast<const uint4*>(a.v + tok * a.v_tok_stride + (int64_t)h * kD) + hl);
+            dst[r] = slot;
+          }
+        }
       }
-      const int64_t tok = tok_start + cand_token(c, blk_start, blk_len);
-      const uint4* ks = reinterpret_cast<const uint4*>(a.k + tok * a.k_tok_stride + (int64_t)h * kD);
-      const uint4* vs = reinterpret_cast<const uint4*>(a.v + tok * a.v_tok_stride + (int64_t)h * kD);
-      uint4* kd = reinterpret_cast<uint4*>(a.k_cache + slot * a.cache_tok_stride + (int64_t)h * kD);
-      uint4* vd = reinterpret_cast<uint4*>(a.v_cache + slot * a.cache_tok_stride + (int64_t)h * kD);
-      kd[hl] = __ldg(ks + hl);
-      vd[hl] = __ldg(vs + hl);
+#pragma unroll
+      for (int r = 0; r < kRowsInFlight; ++r) {
+        if (dst[r] < 0) continue;
+        reinterpret_cast<uint4*>(a.k_cache + dst[r] * a.cache_tok_stride + (int64_t)h * kD)[hl] = kv[r][0];
+        reinterpret_cast<uint4*>(a.v_cache + dst[r] * a.cache_tok_stride + (int64_t)h * kD)[hl] = kv[r][1];
+      }
     }
   } else {
     const int row_vec = a.Hkv * kD / 8;  // uint4 per row
     for (int j = warp; j < n_keep; j += kWarps) {
-      const int c = (int)(0xffffffffu - (uint32_t)(keys[j] & 0xffffffffu));
+      const int c = (int)(0xffffffffu - (uint32_t)(sel[j] & 0xffffffffu));
       const int64_t slot = a.slots[slot_off + j];
       if (slot < 0) continue;
       if (slot >= a.num_slots) {
@@ -207,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kv_kernel(SelectArgs a) {
       const uint4* vs = reinterpret_cast<const uint4*>(a.v + tok * a.v_tok_stride);
       uint4* kd = reinterpret_cast<uint4*>(a.k_cache + slot * a.cache_tok_stride);
       uint4* vd = reinterpret_cast<uint4*>(a.v_cache + slot * a.cache_tok_stride);
+#pragma unroll 8
       for (int e = lane; e < row_vec; e += 32) {
         kd[e] = __ldg(ks + e);
         vd[e] = __ldg(vs + e);
@@ -221,7 +385,7 @@ size_t select_kv_smem_bytes(int nq, int max_klen) {
   int p2 = 1;
   while (p2 < max_klen) p2 <<= 1;
   const size_t head = (((size_t)nq * kD * 4 + (size_t)max_klen * 4 + 15) & ~(size_t)15);
-  return head + (size_t)p2 * 8;
+  return head + (size_t)p2 * 8 + (256 + kWarps + 4) * 4;
 }
 
 cudaError_t launch_select_kv(const SelectArgs& a, bool head_select, int n_seqs, cudaStream_t stream) {
