@@ -218,7 +218,7 @@ DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
 // next unit's Q/K/V and the MMA warp starts its QKs while the softmax warps
 // still write the previous unit's output.
 __global__ void __launch_bounds__(kThreads, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    attn_fwd_split_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
                     const __grid_constant__ CUtensorMap tmVc, AttnKernelArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -695,7 +695,7 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    e = cudaFuncSetAttribute(split::attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(split::attn_fwd_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)split::kSmemBytes);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
@@ -707,7 +707,7 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_units = (int)units;
   const int grid = (int)(units < num_sms ? units : num_sms);
-  split::attn_fwd_kernel<<<grid, split::kThreads, split::kSmemBytes, stream>>>(tmQ, tmK, tmV, tmKc, tmVc, a);
+  split::attn_fwd_split_kernel<<<grid, split::kThreads, split::kSmemBytes, stream>>>(tmQ, tmK, tmV, tmKc, tmVc, a);
   return cudaGetLastError();
 }
 
