@@ -49,9 +49,10 @@ constexpr uint32_t kOffQ = 0;                                   // 2 tiles
 constexpr uint32_t kOffK = kOffQ + 2 * kTileBytes;              // kStagesK tiles
 constexpr uint32_t kOffV = kOffK + kStagesK * kTileBytes;       // kStagesV tiles
 constexpr uint32_t kOffBar = kOffV + kStagesV * kTileBytes;     // barriers
-constexpr uint32_t kNumBars = 2 + 2 * kStagesK + 2 * kStagesV + 2 + 2 + 2 + 1;
+constexpr uint32_t kNumBars = 2 + 2 * kStagesK + 2 * kStagesV + 2 + 2 + 2 + 1 + 2 * 4;  // + unit ring
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
-constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;          // + alignment slack
+constexpr uint32_t kOffRing = kOffMisc + 64;                   // kRing unit ids
+constexpr uint32_t kSmemBytes = kOffRing + 16 + 1024;          // + alignment slack
 
 // barrier indices
 constexpr int BAR_Q = 0;
@@ -64,6 +65,9 @@ constexpr int BAR_SFULL = BAR_VEMPTY + kStagesV;  // 2
 constexpr int BAR_PFULL = BAR_SFULL + 2;         // 2
 constexpr int BAR_OFULL = BAR_PFULL + 2;         // 2
 constexpr int BAR_DRAIN = BAR_OFULL + 2;         // 1
+constexpr int kRing = 4;                         // unit ids published ahead of their use
+constexpr int BAR_UFULL = BAR_DRAIN + 1;         // kRing: unit id published
+constexpr int BAR_UEMPTY = BAR_UFULL + kRing;    // kRing: every role read it
 
 DLLM_DEVICE int row_in_tile_of(int tid) { return tid & 127; }
 
@@ -199,7 +203,13 @@ DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
   return r;
 }
 
-// Persistent kernel: CTA c processes units c, c + gridDim.x, ... Barrier
+// Persistent kernel. Warp 8 (lane 0) chooses the CTA's units and publishes
+// them through a ring of kRing ids in shared memory that every role reads:
+// with a scheduler workspace (args.sched, two int32 words that are zero on
+// entry) CTA c starts at unit c and then claims gridDim.x + atomicAdd(counter)
+// — the CTAs that finish early take the remaining units, which evens out
+// batches of unequal sequence lengths — and the last CTA to exit zeroes the
+// workspace again; without one, CTA c takes c, c + gridDim.x, ... Barrier
 // phases run on across units (ring counters below), so the producer loads the
 // next unit's Q/K/V and the MMA warp starts its QK while the softmax warps
 // still write the previous unit's output.
@@ -242,6 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(BAR_OFULL + i), 1);
     }
     mbar_init(bar(BAR_DRAIN), 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(bar(BAR_UFULL + i), 1);
+      mbar_init(bar(BAR_UEMPTY + i), 10);  // V producer, MMA thread, 8 softmax warps
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -262,6 +276,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  volatile int* uring = reinterpret_cast<volatile int*>(smem + kOffRing);
+  // consumer side: next unit id from the ring (bounded wait); -1 on abort
+  // warp_wide: every lane of the warp calls it (one arrival from lane 0);
+  // otherwise a single thread calls it and arrives itself.
+  auto take_unit = [&](uint32_t n, bool warp_wide) -> int {
+    bool got = mbar_wait(bar(BAR_UFULL + n % kRing), (n / kRing) & 1, abort_flag);
+    if (warp_wide) got = __all_sync(0xffffffffu, got);
+    if (!got) return -1;
+    const int u = uring[n % kRing];
+    if (warp_wide) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_UEMPTY + n % kRing));
+    } else {
+      mbar_arrive(bar(BAR_UEMPTY + n % kRing));
+    }
+    return u;
+  };
   if (threadIdx.x == 9 * 32) TRACE(1, 0, 0);
 
   if (warp == 8 || warp == 10) {
@@ -280,10 +311,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const __nv_bfloat16* cache = kq ? args.kc : args.vc;
     uint32_t q_it = 0;     // units whose Q was loaded (warp 8)
     uint32_t done = 0;     // tiles issued into this ring
+    int next_static = (int)blockIdx.x + (int)gridDim.x;  // static order (warp 8, lane 0)
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    for (uint32_t n = 0; ok; ++n) {
+      int u;
+      if (kq) {
+        // claim the next valid unit: the first is blockIdx.x, later ones from the counter
+        if (n >= (uint32_t)kRing) ok = mbar_wait(bar(BAR_UEMPTY + n % kRing), (n / kRing - 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        if (lane == 0) {
+          // Dynamic: every CTA starts at unit blockIdx.x and then claims units
+          // gridDim.x, gridDim.x + 1, ... from the counter (fast CTAs take more).
+          // Static: units blockIdx.x + i * gridDim.x.
+          auto claim = [&]() -> int {
+            if (args.sched != nullptr) return (int)gridDim.x + atomicAdd(&args.sched[0], 1);
+            const int r = next_static;
+            next_static += (int)gridDim.x;
+            return r;
+          };
+          u = n == 0 ? (int)blockIdx.x : claim();
+          while (u < total_units && !decode_unit(u, args).valid) u = claim();
+          uring[n % kRing] = u < total_units ? u : -2;
+          mbar_arrive(bar(BAR_UFULL + n % kRing));
+        }
+        u = __shfl_sync(0xffffffffu, u, 0);
+        if (u >= total_units) break;
+      } else {
+        u = take_unit(n, true);
+        if (u == -1) { ok = false; break; }
+        if (u < 0) break;
+      }
       const Unit t = decode_unit(u, args);
-      if (!t.valid) continue;
       if (kq) {
         if (q_it > 0) ok = mbar_wait(bar(BAR_QEMPTY), (q_it - 1) & 1, abort_flag);
         if (!ok) break;
@@ -408,9 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t q_it = 0, kv_it = 0;
       uint32_t p_it[2] = {0, 0};
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      for (uint32_t n = 0; ok; ++n) {
+        const int u = take_unit(n, false);
+        if (u == -1) { ok = false; break; }
+        if (u < 0) break;
         const Unit t = decode_unit(u, args);
-        if (!t.valid) continue;
         ok = mbar_wait(bar(BAR_Q), q_it & 1, abort_flag);
         if (!ok) break;
         ++q_it;
@@ -487,9 +548,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = args.scale_log2;
     uint32_t s_it = 0, o_it = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    for (uint32_t n = 0; ok; ++n) {
+      const int u = take_unit(n, true);
+      if (u == -1) { ok = false; break; }
+      if (u < 0) break;
       const Unit t = decode_unit(u, args);
-      if (!t.valid || wg >= t.ntiles) continue;
+      if (wg >= t.ntiles) continue;
       float m = -INFINITY;
       float l = 0.f;
       for (int j = 0; j < t.nkv; ++j) {
@@ -616,6 +680,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem, 512);
   }
   if (threadIdx.x == 0 && *abort_flag) set_error(args.err, kDevWaitTimeout);
+  if (threadIdx.x == 0 && args.sched != nullptr) {
+    // The last CTA to finish (every CTA has stopped claiming) returns the
+    // workspace to zero for the next launch on the stream.
+    __threadfence();
+    if (atomicAdd(&args.sched[1], 1) == (int)gridDim.x - 1) {
+      atomicExch(&args.sched[0], 0);
+      atomicExch(&args.sched[1], 0);
+    }
+  }
 }
 
 uint32_t attn_fwd_smem_bytes() { return kSmemBytes; }

@@ -29,6 +29,10 @@ struct AttnKernelArgs {
   const __nv_bfloat16* kc;
   const __nv_bfloat16* vc;
   int64_t c_tok_stride;    // elements between cache slots
+  // Optional scheduler workspace (pair kernel): two int32 words, zero on entry,
+  // zero again when the kernel exits. Launches that may run at the same time
+  // need distinct workspaces. Null: static round-robin unit order.
+  int32_t* sched;
   int qunits;              // query units per (sequence, head): 256-row tile pairs (pair
                            // kernel) or 128-row tiles (split kernel); set by the launcher
   int total_units;         // B * Hq * qunits; set by the launcher

@@ -104,7 +104,7 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
                 const void* vc, int64_t vc_tok_stride, void* o, int64_t o_tok_stride,
                 const int32_t* cu_q, const int32_t* cu_k, const int32_t* cu_c, int batch,
                 int max_q, int64_t total_q, int64_t total_k, int64_t total_c, int Hq, int Hkv,
-                int head_dim, float scale, int32_t* err, void* stream,
+                int head_dim, float scale, int32_t* sched, int32_t* err, void* stream,
                 const int32_t* slots = nullptr) {
   if (head_dim != 128)
     return fail(DLLM_ERR_UNSUPPORTED, "head_dim %d not supported (only 128)", head_dim);
@@ -158,6 +158,7 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.kc = reinterpret_cast<const __nv_bfloat16*>(kc);
   a.vc = reinterpret_cast<const __nv_bfloat16*>(vc);
   a.c_tok_stride = kc_tok_stride;
+  a.sched = sched;
   a.qunits = 0;
   a.total_units = 0;
   // Query segments that fit one tile (the reuse steps' fresh blocks) go to the
@@ -238,12 +239,12 @@ int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const void* k, int
                          const void* v, int64_t v_tok_stride, void* o, int64_t o_tok_stride,
                          const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
                          int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
-                         int num_kv_heads, int head_dim, float softmax_scale, int32_t* err_flag,
-                         void* stream) {
+                         int num_kv_heads, int head_dim, float softmax_scale,
+                         int32_t* sched_workspace, int32_t* err_flag, void* stream) {
   return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, nullptr, 0, nullptr, 0, o,
                      o_tok_stride, cu_seqlens_q, cu_seqlens_k, nullptr, batch, max_seqlen_q,
                      total_q, total_k, 0, num_heads, num_kv_heads, head_dim, softmax_scale,
-                     err_flag, stream);
+                     sched_workspace, err_flag, stream);
 }
 
 int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, const void* k,
@@ -254,12 +255,12 @@ int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, const void*
                                 const int32_t* cu_seqlens_c, int batch, int max_seqlen_q,
                                 int64_t total_q, int64_t total_k, int64_t total_c, int num_heads,
                                 int num_kv_heads, int head_dim, float softmax_scale,
-                                int32_t* err_flag, void* stream) {
+                                int32_t* sched_workspace, int32_t* err_flag, void* stream) {
   if (cu_seqlens_c == nullptr) return fail(DLLM_ERR_INVALID_ARG, "cu_seqlens_c is null");
   return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, kc, kc_tok_stride, vc,
                      vc_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k, cu_seqlens_c,
                      batch, max_seqlen_q, total_q, total_k, total_c, num_heads, num_kv_heads,
-                     head_dim, softmax_scale, err_flag, stream);
+                     head_dim, softmax_scale, sched_workspace, err_flag, stream);
 }
 
 int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, const void* k,
@@ -270,14 +271,14 @@ int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, const void* 
                                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
                                int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
                                int num_kv_heads, int head_dim, float softmax_scale,
-                               int32_t* err_flag, void* stream) {
+                               int32_t* sched_workspace, int32_t* err_flag, void* stream) {
   if (cu_seqlens_slots == nullptr || slots == nullptr)
     return fail(DLLM_ERR_INVALID_ARG, "slots / cu_seqlens_slots is null");
   if (num_slots <= 0) return fail(DLLM_ERR_INVALID_ARG, "num_slots must be > 0");
   return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, k_cache, cache_tok_stride,
                      v_cache, cache_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k,
                      cu_seqlens_slots, batch, max_seqlen_q, total_q, total_k, num_slots, num_heads,
-                     num_kv_heads, head_dim, softmax_scale, err_flag, stream, slots);
+                     num_kv_heads, head_dim, softmax_scale, sched_workspace, err_flag, stream, slots);
 }
 
 int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,

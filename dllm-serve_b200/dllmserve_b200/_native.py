@@ -23,6 +23,7 @@ DLLM_DEV_WAIT_TIMEOUT = 2
 DLLM_DEV_BAD_SEQUENCE = 3
 
 SEQ_DESC_INTS = 8
+SCHED_WORKSPACE_INTS = 2  # DLLM_SCHED_WORKSPACE_INTS
 
 # Every exported entry point with its (argtypes, restype).
 _P = ctypes.c_void_p
@@ -35,17 +36,17 @@ SIGNATURES = {
     "dllm_store_kvcache": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _I64, _I, _I64, _P, _P], _I),
     "dllm_load_kvcache": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _I64, _I, _I64, _P, _P], _I),
     "dllm_attn_varlen_fwd": (
-        [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _I, _I, _I, _F, _P, _P],
+        [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _I, _I, _I, _F, _P, _P, _P],
         _I,
     ),
     "dllm_attn_varlen_cached_fwd": (
         [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _I, _I64, _I64,
-         _I64, _I, _I, _I, _F, _P, _P],
+         _I64, _I, _I, _I, _F, _P, _P, _P],
         _I,
     ),
     "dllm_attn_varlen_paged_fwd": (
         [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _I, _I, _I64,
-         _I64, _I, _I, _I, _F, _P, _P],
+         _I64, _I, _I, _I, _F, _P, _P, _P],
         _I,
     ),
     "dllm_select_kv_store": (

@@ -29,6 +29,16 @@ def device_status_word(device: torch.device) -> torch.Tensor:
     return t
 
 
+def _status_ptr(device: torch.device) -> int:
+    """Pointer of the status word, or 0 (no device status) when none exists yet
+    and the current stream is being captured (memory allocated during a
+    capture belongs to that graph and must not be cached)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _STATUS and torch.cuda.is_current_stream_capturing():
+        return 0
+    return device_status_word(device).data_ptr()
+
+
 def read_device_status(device: torch.device, reset: bool = True) -> int:
     """Synchronising read of the device status word (tests / debug only)."""
     t = device_status_word(device)
@@ -104,7 +114,7 @@ def _kv_copy(store, key, value, k_cache, v_cache, slot_mapping, D):
             key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
             k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr(),
             N, D, key.element_size(), num_slots,
-            device_status_word(dev).data_ptr(), _stream_ptr(),
+            _status_ptr(dev), _stream_ptr(),
         )
     _native.check(rc, "store_kvcache" if store else "load_kvcache")
     LAUNCHES[0] += 1
@@ -120,6 +130,27 @@ def _check_rows(name, t, heads, head_dim):
         raise ValueError(f"{name} must be bfloat16")
     if t.stride(2) != 1 or t.stride(1) != head_dim:
         raise ValueError(f"{name} must have contiguous heads (strides [*, {head_dim}, 1])")
+
+
+_SCHED_WS: dict = {}
+
+
+def sched_workspace(dev: torch.device) -> int:
+    """Device pointer of the attention scheduler workspace of ``dev`` (zeroed
+    int32 words the kernel leaves zero), or 0 (round-robin order) when none
+    exists yet and the current stream is being captured: memory allocated
+    during a capture belongs to that graph and must not be cached. One
+    workspace per device: attention launches of this package on one device
+    are stream-ordered (concurrent launches on several streams would need one
+    workspace each)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _SCHED_WS.get(idx)
+    if ws is None:
+        if torch.cuda.is_current_stream_capturing():
+            return 0
+        ws = torch.zeros(_native.SCHED_WORKSPACE_INTS, dtype=torch.int32, device=torch.device("cuda", idx))
+        _SCHED_WS[idx] = ws
+    return ws.data_ptr()
 
 
 def varlen_attention(
@@ -165,8 +196,9 @@ def varlen_attention(
         if out.shape[0] != q.shape[0]:
             raise ValueError("out must have as many rows as q")
     lib = _native.lib()
-    status = device_status_word(dev).data_ptr()
+    status = _status_ptr(dev)
     with torch.cuda.device(dev):
+        sched = sched_workspace(dev)
         if k_cache is not None:
             _require_cuda(q, k_cache, v_cache, slots, cu_seqlens_slots)
             if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
@@ -185,14 +217,14 @@ def varlen_attention(
                 k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row,
                 slots.data_ptr(), cu_seqlens_slots.data_ptr(), out.data_ptr(), out.stride(0),
                 cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), B, int(max_seqlen_q), q.shape[0],
-                k.shape[0], Hq, Hkv, D, float(softmax_scale), status, _stream_ptr(),
+                k.shape[0], Hq, Hkv, D, float(softmax_scale), sched, status, _stream_ptr(),
             )
         elif k_cached is None:
             rc = lib.dllm_attn_varlen_fwd(
                 q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
                 out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
                 B, int(max_seqlen_q), q.shape[0], k.shape[0], Hq, Hkv, D, float(softmax_scale),
-                status, _stream_ptr(),
+                sched, status, _stream_ptr(),
             )
         else:
             _check_rows("k_cached", k_cached, Hkv, D)
@@ -207,7 +239,7 @@ def varlen_attention(
                 k_cached.data_ptr(), k_cached.stride(0), v_cached.data_ptr(), v_cached.stride(0),
                 out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
                 cu_seqlens_c.data_ptr(), B, int(max_seqlen_q), q.shape[0], k.shape[0],
-                k_cached.shape[0], Hq, Hkv, D, float(softmax_scale), status, _stream_ptr(),
+                k_cached.shape[0], Hq, Hkv, D, float(softmax_scale), sched, status, _stream_ptr(),
             )
     _native.check(rc, "varlen_attention")
     if B > 0 and q.shape[0] > 0:
@@ -258,7 +290,7 @@ def select_kv_store(
             q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
             seq_desc.data_ptr(), seq_desc.shape[0], int(max_klen), Hq, Hkv, D, int(bool(head_select)),
             k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row, slots.data_ptr(),
-            _ptr(top_idx), device_status_word(dev).data_ptr(), _stream_ptr(),
+            _ptr(top_idx), _status_ptr(dev), _stream_ptr(),
         )
     _native.check(rc, "select_kv_store")
     if seq_desc.shape[0] > 0 and max_klen > 0:

@@ -33,6 +33,12 @@
  *     one-line message for the calling thread.
  *   - `err_flag` (optional, int32 device word) receives a device-side status: the first
  *     nonzero DLLM_DEV_* code seen by any kernel thread. The caller clears and reads it.
+ *   - `sched_workspace` (optional, attention entry points): DLLM_SCHED_WORKSPACE_INTS int32
+ *     device words, zero before their first use. With it, launches whose query segments
+ *     exceed 128 rows hand out their work units dynamically (an atomic counter) instead of
+ *     round-robin, which evens out batches of unequal lengths; the kernel returns the words
+ *     to zero when it exits. Launches that may run at the same time (other streams) need
+ *     distinct workspaces. NULL: round-robin order (same results, bit for bit).
  */
 #ifndef DLLM_ATTN_H_
 #define DLLM_ATTN_H_
@@ -56,6 +62,9 @@ extern "C" {
 #define DLLM_ERR_ALIGNMENT 3     /* pointer or stride not aligned for vector/TMA access */
 #define DLLM_ERR_TOO_LARGE 4     /* a size beyond the kernel's limit */
 #define DLLM_ERR_CUDA 5          /* CUDA launch / driver error */
+
+/* int32 words of an attention scheduler workspace */
+#define DLLM_SCHED_WORKSPACE_INTS 2
 
 /* device-side status codes written to err_flag */
 #define DLLM_DEV_SLOT_OUT_OF_RANGE 1
@@ -105,8 +114,8 @@ DLLM_API int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const voi
                          const void* v, int64_t v_tok_stride, void* o, int64_t o_tok_stride,
                          const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
                          int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
-                         int num_kv_heads, int head_dim, float softmax_scale, int32_t* err_flag,
-                         void* stream);
+                         int num_kv_heads, int head_dim, float softmax_scale,
+                         int32_t* sched_workspace, int32_t* err_flag, void* stream);
 
 /*
  * As dllm_attn_varlen_fwd, but the keys/values of sequence b are the
@@ -124,7 +133,8 @@ DLLM_API int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, co
                                 const int32_t* cu_seqlens_c, int batch, int max_seqlen_q,
                                 int64_t total_q, int64_t total_k, int64_t total_c,
                                 int num_heads, int num_kv_heads, int head_dim,
-                                float softmax_scale, int32_t* err_flag, void* stream);
+                                float softmax_scale, int32_t* sched_workspace, int32_t* err_flag,
+                                void* stream);
 
 /*
  * As dllm_attn_varlen_cached_fwd, but the cached keys/values of sequence b are read
@@ -145,7 +155,7 @@ DLLM_API int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, con
                                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
                                int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
                                int num_kv_heads, int head_dim, float softmax_scale,
-                               int32_t* err_flag, void* stream);
+                               int32_t* sched_workspace, int32_t* err_flag, void* stream);
 
 /*
  * Per-sequence descriptor for dllm_select_kv_store: 8 int32 values per sequence.

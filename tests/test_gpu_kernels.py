@@ -180,6 +180,39 @@ def test_attention_many_sequences(dev, batch):
     _status_clear(dev)
 
 
+def test_attention_sched_workspace_matches_round_robin(dev):
+    """Dynamic unit scheduling (a scheduler workspace) writes the same output
+    bits as the round-robin order, twice in a row, and leaves the workspace zero."""
+    import ctypes
+    from dllmserve_b200 import _native
+    g = I.gen(140)
+    D, H = 128, 8
+    lens = [419, 1087, 700, 130, 900, 256, 555, 1000, 3]
+    N = sum(lens)
+    q, k, v = (I.normal(g, (N, H, D)).to(dev, torch.bfloat16) for _ in range(3))
+    cu = torch.tensor(_cu(lens), dtype=torch.int32, device=dev)
+    lib = _native.lib()
+
+    def run(ws):
+        o = torch.full_like(q, float("nan"))
+        rc = lib.dllm_attn_varlen_fwd(
+            q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+            o.data_ptr(), o.stride(0), cu.data_ptr(), cu.data_ptr(), len(lens), max(lens), N, N,
+            H, H, D, ctypes.c_float(D ** -0.5), None if ws is None else ws.data_ptr(), None,
+            torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, lib.dllm_last_error()
+        return o
+
+    ref = run(None)
+    ws = torch.zeros(_native.SCHED_WORKSPACE_INTS, dtype=torch.int32, device=dev)
+    first, second = run(ws), run(ws)
+    torch.cuda.synchronize()
+    assert torch.equal(first, ref) and torch.equal(second, ref)
+    assert int(ws.abs().sum()) == 0
+    _check_attn(ref, R.varlen_attention(q.float().cpu(), k.float().cpu(), v.float().cpu(),
+                                        _cu(lens), _cu(lens), D ** -0.5))
+
+
 def test_attention_fused_qkv_views(dev):
     """q/k/v as strided views of one fused projection output."""
     g = I.gen(78)

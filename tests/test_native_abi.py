@@ -41,25 +41,25 @@ def test_validation_errors_without_gpu():
     lib = _native.lib()
     # head_dim 64 is rejected before any device work
     rc = lib.dllm_attn_varlen_fwd(None, 0, None, 0, None, 0, None, 0, None, None, 1, 1, 1, 1,
-                                  4, 4, 64, ctypes.c_float(0.1), None, None)
+                                  4, 4, 64, ctypes.c_float(0.1), None, None, None)
     assert rc == _native.DLLM_ERR_UNSUPPORTED
     assert "head_dim" in lib.dllm_last_error().decode()
     # GQA ratio must divide
     rc = lib.dllm_attn_varlen_fwd(None, 0, None, 0, None, 0, None, 0, None, None, 1, 1, 1, 1,
-                                  6, 4, 128, ctypes.c_float(0.1), None, None)
+                                  6, 4, 128, ctypes.c_float(0.1), None, None, None)
     assert rc == _native.DLLM_ERR_UNSUPPORTED
     # non-positive scale
     rc = lib.dllm_attn_varlen_fwd(None, 0, None, 0, None, 0, None, 0, None, None, 1, 1, 1, 1,
-                                  4, 4, 128, ctypes.c_float(0.0), None, None)
+                                  4, 4, 128, ctypes.c_float(0.0), None, None, None)
     assert rc == _native.DLLM_ERR_INVALID_ARG
     # empty batch is a no-op
     rc = lib.dllm_attn_varlen_fwd(None, 0, None, 0, None, 0, None, 0, None, None, 0, 0, 0, 0,
-                                  4, 4, 128, ctypes.c_float(0.1), None, None)
+                                  4, 4, 128, ctypes.c_float(0.1), None, None, None)
     assert rc == _native.DLLM_OK
     # cached variant needs cu_seqlens_c
     rc = lib.dllm_attn_varlen_cached_fwd(None, 0, None, 0, None, 0, None, 0, None, 0, None, 0,
                                          None, None, None, 1, 1, 1, 1, 1, 4, 4, 128,
-                                         ctypes.c_float(0.1), None, None)
+                                         ctypes.c_float(0.1), None, None, None)
     assert rc == _native.DLLM_ERR_INVALID_ARG
     # kv copies
     rc = lib.dllm_store_kvcache(None, 0, None, 0, None, None, None, 0, 8, 2, 1, None, None)
