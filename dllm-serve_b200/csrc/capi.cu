@@ -211,6 +211,27 @@ int kv_copy_common(bool store, const void* key, int64_t key_stride, const void* 
   return DLLM_OK;
 }
 
+// Scheduler workspace of dllm_attn_varlen_fwd_static_ws: file-scope device
+// memory (one copy per device, zero when the module loads). The attention
+// kernel uses the first DLLM_SCHED_WORKSPACE_INTS words and leaves them zero.
+constexpr int kStaticWsInts = 64;
+static __device__ __align__(256) int32_t g_static_sched_ws[kStaticWsInts];
+
+// Device address of g_static_sched_ws on the current device, looked up once
+// per device; nullptr (and the CUDA error in *e) if the lookup fails.
+int32_t* static_sched_ws(cudaError_t* e) {
+  static int32_t* addr[64] = {nullptr};
+  int dev = 0;
+  *e = cudaGetDevice(&dev);
+  if (*e != cudaSuccess) return nullptr;
+  if (dev >= 0 && dev < 64 && addr[dev] != nullptr) return addr[dev];
+  void* p = nullptr;
+  *e = cudaGetSymbolAddress(&p, g_static_sched_ws);
+  if (*e != cudaSuccess) return nullptr;
+  if (dev >= 0 && dev < 64) addr[dev] = static_cast<int32_t*>(p);
+  return static_cast<int32_t*>(p);
+}
+
 }  // namespace
 
 extern "C" {
@@ -245,6 +266,26 @@ int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const void* k, int
                      o_tok_stride, cu_seqlens_q, cu_seqlens_k, nullptr, batch, max_seqlen_q,
                      total_q, total_k, 0, num_heads, num_kv_heads, head_dim, softmax_scale,
                      sched_workspace, err_flag, stream);
+}
+
+int dllm_attn_varlen_fwd_static_ws(const void* q, int64_t q_tok_stride, const void* k,
+                                   int64_t k_tok_stride, const void* v, int64_t v_tok_stride,
+                                   void* o, int64_t o_tok_stride, const int32_t* cu_seqlens_q,
+                                   const int32_t* cu_seqlens_k, int batch, int max_seqlen_q,
+                                   int64_t total_q, int64_t total_k, int num_heads,
+                                   int num_kv_heads, int head_dim, float softmax_scale,
+                                   int32_t* err_flag, void* stream) {
+  static_assert(DLLM_SCHED_WORKSPACE_INTS <= kStaticWsInts, "static workspace too small");
+  if (DLLM_SCHED_WORKSPACE_INTS > kStaticWsInts)
+    return fail(DLLM_ERR_TOO_LARGE, "scheduler workspace needs %d words > %d", DLLM_SCHED_WORKSPACE_INTS,
+                kStaticWsInts);
+  cudaError_t e = cudaSuccess;
+  int32_t* ws = static_sched_ws(&e);
+  if (ws == nullptr) return cuda_fail(e, "cudaGetSymbolAddress(static scheduler workspace)");
+  return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, nullptr, 0, nullptr, 0, o,
+                     o_tok_stride, cu_seqlens_q, cu_seqlens_k, nullptr, batch, max_seqlen_q,
+                     total_q, total_k, 0, num_heads, num_kv_heads, head_dim, softmax_scale, ws,
+                     err_flag, stream);
 }
 
 int dllm_attn_varlen_cached_fwd(const void* q, int64_t q_tok_stride, const void* k,

@@ -39,6 +39,10 @@ SIGNATURES = {
         [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _I, _I, _I, _F, _P, _P, _P],
         _I,
     ),
+    "dllm_attn_varlen_fwd_static_ws": (
+        [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I, _I, _I64, _I64, _I, _I, _I, _F, _P, _P],
+        _I,
+    ),
     "dllm_attn_varlen_cached_fwd": (
         [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I, _I, _I64, _I64,
          _I64, _I, _I, _I, _F, _P, _P, _P],

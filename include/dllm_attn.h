@@ -118,6 +118,25 @@ DLLM_API int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const voi
                          int32_t* sched_workspace, int32_t* err_flag, void* stream);
 
 /*
+ * dllm_attn_varlen_fwd with its scheduler workspace taken from memory the library
+ * owns: a file-scope static device array of 64 int32 words (one per device, zero
+ * when the library loads; the call uses the first DLLM_SCHED_WORKSPACE_INTS and the
+ * kernel returns them to zero on exit). Allocates nothing; the array's address is
+ * looked up once per device with cudaGetSymbolAddress (the device current at the
+ * call). Returns DLLM_ERR_TOO_LARGE if a workspace would not fit the array.
+ * Calls that overlap in time on one device (several streams or threads) share
+ * the words and race: run them one after another. No reference counterpart: the
+ * reference's flash_attn_varlen_func has no scheduler workspace.
+ */
+DLLM_API int dllm_attn_varlen_fwd_static_ws(const void* q, int64_t q_tok_stride, const void* k,
+                                   int64_t k_tok_stride, const void* v, int64_t v_tok_stride,
+                                   void* o, int64_t o_tok_stride, const int32_t* cu_seqlens_q,
+                                   const int32_t* cu_seqlens_k, int batch, int max_seqlen_q,
+                                   int64_t total_q, int64_t total_k, int num_heads,
+                                   int num_kv_heads, int head_dim, float softmax_scale,
+                                   int32_t* err_flag, void* stream);
+
+/*
  * As dllm_attn_varlen_fwd, but the keys/values of sequence b are the
  * concatenation [cached rows cu_seqlens_c[b]..cu_seqlens_c[b+1] of kc/vc ;
  * fresh rows cu_seqlens_k[b]..cu_seqlens_k[b+1] of k/v], without materialising
