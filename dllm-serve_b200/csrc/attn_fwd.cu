@@ -281,8 +281,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // warp_wide: every lane of the warp calls it (one arrival from lane 0);
   // otherwise a single thread calls it and arrives itself.
   auto take_unit = [&](uint32_t n, bool warp_wide) -> int {
-    bool got = mbar_wait(bar(BAR_UFULL + n % kRing), (n / kRing) & 1, abort_flag);
-    if (warp_wide) got = __all_sync(0xffffffffu, got);
+    const bool got = warp_wide ? mbar_wait_warp(bar(BAR_UFULL + n % kRing), (n / kRing) & 1, abort_flag)
+                               : mbar_wait(bar(BAR_UFULL + n % kRing), (n / kRing) & 1, abort_flag);
     if (!got) return -1;
     const int u = uring[n % kRing];
     if (warp_wide) {
@@ -317,8 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int u;
       if (kq) {
         // claim the next valid unit: the first is blockIdx.x, later ones from the counter
-        if (n >= (uint32_t)kRing) ok = mbar_wait(bar(BAR_UEMPTY + n % kRing), (n / kRing - 1) & 1, abort_flag);
-        ok = __all_sync(0xffffffffu, ok);
+        if (n >= (uint32_t)kRing) ok = mbar_wait_warp(bar(BAR_UEMPTY + n % kRing), (n / kRing - 1) & 1, abort_flag);
         if (!ok) break;
         if (lane == 0) {
           // Dynamic: every CTA starts at unit blockIdx.x and then claims units
@@ -344,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const Unit t = decode_unit(u, args);
       if (kq) {
-        if (q_it > 0) ok = mbar_wait(bar(BAR_QEMPTY), (q_it - 1) & 1, abort_flag);
+        if (q_it > 0) ok = mbar_wait_warp(bar(BAR_QEMPTY), (q_it - 1) & 1, abort_flag);
         if (!ok) break;
         if (lane == 0) {
           mbar_arrive_expect_tx(bar(BAR_Q), t.ntiles * kTileBytes);
@@ -360,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < t.nkv; ++j) {
         const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
         const int st = done % nst;
-        if (done >= (uint32_t)nst) ok = mbar_wait(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
+        if (done >= (uint32_t)nst) ok = mbar_wait_warp(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
         if (!ok) break;
         const uint32_t dk = ring + st * kTileBytes;
         if (kt.seg == 0 && args.slots != nullptr) {
@@ -558,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float l = 0.f;
       for (int j = 0; j < t.nkv; ++j) {
         const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
-        ok = mbar_wait(bar(BAR_SFULL + wg), s_it & 1, abort_flag);
+        ok = mbar_wait_warp(bar(BAR_SFULL + wg), s_it & 1, abort_flag);
         if (!ok) break;
         ++s_it;
         if (row_in_tile == 0) TRACE(10, j, wg);
@@ -637,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __nv_bfloat16* orow = args.o + (int64_t)(t.q_begin + row) * args.o_tok_stride +
                             (int64_t)t.hq * args.o_head_stride;
       if (t.nkv > 0) {
-        ok = mbar_wait(bar(BAR_OFULL + wg), o_it & 1, abort_flag);
+        ok = mbar_wait_warp(bar(BAR_OFULL + wg), o_it & 1, abort_flag);
         if (!ok) break;
         ++o_it;
         if (row_in_tile == 0) TRACE(14, 0, wg);

@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (kq) {
         const int qs = q_it % kStagesQ;
         if (q_it >= (uint32_t)kStagesQ)
-          ok = mbar_wait(bar(BAR_QEMPTY + qs), (q_it / kStagesQ - 1) & 1, abort_flag);
+          ok = mbar_wait_warp(bar(BAR_QEMPTY + qs), (q_it / kStagesQ - 1) & 1, abort_flag);
         if (!ok) break;
         if (lane == 0) {
           const uint32_t dst = base + kOffQ + qs * kTileBytes;
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < t.nkv; ++j) {
         const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
         const int st = done % nst;
-        if (done >= (uint32_t)nst) ok = mbar_wait(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
+        if (done >= (uint32_t)nst) ok = mbar_wait_warp(bar(bempty + st), (done / nst - 1) & 1, abort_flag);
         if (!ok) break;
         const uint32_t dk = ring + st * kTileBytes;
         if (kt.seg == 0 && args.slots != nullptr) {
@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < t.nkv; ++j, ++g) {
         const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
         const uint32_t sb = g & 1;
-        ok = mbar_wait(bar(BAR_SFULL + sb), (g >> 1) & 1, abort_flag);
+        ok = mbar_wait_warp(bar(BAR_SFULL + sb), (g >> 1) & 1, abort_flag);
         if (!ok) break;
         if (row_in_tile == 0) TRACE(10, j, wg);
         tc_fence_after();
@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // The accumulator must hold every PV up to tile g-1: PV(g-2)
               // completed before S(g) did, so one more completion of OREADY
               // (parity of tile g-1) is all there is to wait for.
-              ok = mbar_wait(bar(BAR_OREADY), (g - 1) & 1, abort_flag);
+              ok = mbar_wait_warp(bar(BAR_OREADY), (g - 1) & 1, abort_flag);
               if (!ok) break;
               tc_fence_after();
 #pragma unroll
@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __nv_bfloat16* orow = args.o + (int64_t)(t.q_begin + row) * args.o_tok_stride +
                             (int64_t)t.hq * args.o_head_stride + wg * kHalfN;
       if (t.nkv > 0) {
-        ok = mbar_wait(bar(BAR_OFULL), o_it & 1, abort_flag);
+        ok = mbar_wait_warp(bar(BAR_OFULL), o_it & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         // Merge factors: O = ca * O_a + cb * O_b with ca = 2^(m0-m)/L,
@@ -614,13 +614,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (wg == 1) {
           xch[row_in_tile] = make_float2(m, l);
           mbar_arrive(bar(BAR_XML));
-          ok = mbar_wait(bar(BAR_XF), o_it & 1, abort_flag);
+          ok = mbar_wait_warp(bar(BAR_XF), o_it & 1, abort_flag);
           if (!ok) break;
           const float2 f = xch[row_in_tile];
           ca = f.x;
           cb = f.y;
         } else {
-          ok = mbar_wait(bar(BAR_XML), o_it & 1, abort_flag);
+          ok = mbar_wait_warp(bar(BAR_XML), o_it & 1, abort_flag);
           if (!ok) break;
           const float2 o1 = xch[row_in_tile];
           const float mm = fmaxf(m, o1.x);

@@ -106,6 +106,13 @@ DLLM_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
   }
 }
 
+// mbar_wait called by all 32 lanes of a warp: the lanes agree on the outcome,
+// so a timeout seen by one lane cannot split the warp before a warp-wide
+// operation (shuffle, vote, __syncwarp) that would then never complete.
+DLLM_DEVICE bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort));
+}
+
 // Bounded wait used while draining after an abort: never raises abort.
 DLLM_DEVICE bool mbar_wait_drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   uint64_t t0 = globaltimer_ns();
