@@ -385,6 +385,32 @@ def run_ours(args, lens):
                     "frac_of_hbm": gbs / hbm, "bytes_per_launch": byts, "rows": N,
                     "row_bytes": row * 2}
 
+    # ---------------- rotary embedding of q and k (the op before attention) ----------------
+    rope_block = None
+    if not args.skip_extras:
+        from dllmserve_b200.layers.rotary_embedding import RotaryEmbedding
+
+        rope = RotaryEmbedding(HEAD_DIM, HEAD_DIM, 4096, 500000.0).to(dev)
+        pos = torch.cat([torch.arange(L, device=dev) for L in lens])
+        qo, ko = torch.empty_like(qs[0]), torch.empty_like(ks[0])
+        for _ in range(3):
+            ops.rope_neox(pos, qs[0], ks[0], rope.cos_sin_cache, query_out=qo, key_out=ko)
+        reps = 20
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for r in range(reps):
+            l = r % LAYERS
+            ops.rope_neox(pos, qs[l], ks[l], rope.cos_sin_cache, query_out=qo, key_out=ko)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        byts = N * (Hq + Hk) * HEAD_DIM * 2 * 2 + 8 * N  # q, k read + written, positions
+        gbs = byts / (ms * 1e-3) / 1e9
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        rope_block = {"kernel": "dllm::rope_kernel", "ms": ms, "GB/s": gbs, "frac_of_hbm": gbs / hbm,
+                      "bytes_per_launch": byts, "tokens": N}
+
     # ---------------- TP layer: attention + o_proj + all-reduce ----------------
     tp_block = None
     if not args.skip_extras:
@@ -502,7 +528,7 @@ def run_ours(args, lens):
             "config": config_block(lens, world),
             "step_tokens_per_s": tokens_per_s,
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": launches, "kv_store": kv_block, "tp_layer": tp_block,
+            "gpu_launches": launches, "kv_store": kv_block, "rope": rope_block, "tp_layer": tp_block,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

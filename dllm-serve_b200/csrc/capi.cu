@@ -10,6 +10,7 @@
 #include "attn_fwd.h"
 #include "kvcache.h"
 #include "select_kv.h"
+#include "rope.h"
 
 namespace {
 
@@ -320,6 +321,50 @@ int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, const void* 
                      v_cache, cache_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k,
                      cu_seqlens_slots, batch, max_seqlen_q, total_q, total_k, num_slots, num_heads,
                      num_kv_heads, head_dim, softmax_scale, sched_workspace, err_flag, stream, slots);
+}
+
+int dllm_rope_neox(const int64_t* positions, const void* q_in, int64_t q_in_stride, void* q_out,
+                   int64_t q_out_stride, const void* k_in, int64_t k_in_stride, void* k_out,
+                   int64_t k_out_stride, const float* cos_sin_cache, int64_t max_position,
+                   int64_t n_tokens, int num_heads, int num_kv_heads, int head_dim,
+                   int32_t* err_flag, void* stream) {
+  if (head_dim != 128)
+    return fail(DLLM_ERR_UNSUPPORTED, "head_dim %d not supported (only 128)", head_dim);
+  if (n_tokens < 0 || num_heads < 0 || num_kv_heads < 0 || max_position < 0)
+    return fail(DLLM_ERR_INVALID_ARG, "negative size");
+  if (n_tokens == 0 || num_heads + num_kv_heads == 0) return DLLM_OK;
+  if (positions == nullptr || cos_sin_cache == nullptr)
+    return fail(DLLM_ERR_INVALID_ARG, "positions / cos_sin_cache is null");
+  if ((reinterpret_cast<uintptr_t>(cos_sin_cache) & 15) != 0)
+    return fail(DLLM_ERR_ALIGNMENT, "cos_sin_cache must be 16-byte aligned");
+  int rc;
+  if (num_heads > 0) {
+    if ((rc = check_rows("q_in", q_in, q_in_stride, num_heads, n_tokens)) != DLLM_OK) return rc;
+    if ((rc = check_rows("q_out", q_out, q_out_stride, num_heads, n_tokens)) != DLLM_OK) return rc;
+  }
+  if (num_kv_heads > 0) {
+    if ((rc = check_rows("k_in", k_in, k_in_stride, num_kv_heads, n_tokens)) != DLLM_OK) return rc;
+    if ((rc = check_rows("k_out", k_out, k_out_stride, num_kv_heads, n_tokens)) != DLLM_OK) return rc;
+  }
+  dllm::RopeArgs a;
+  a.positions = positions;
+  a.q_in = reinterpret_cast<const __nv_bfloat16*>(q_in);
+  a.q_out = reinterpret_cast<__nv_bfloat16*>(q_out);
+  a.k_in = reinterpret_cast<const __nv_bfloat16*>(k_in);
+  a.k_out = reinterpret_cast<__nv_bfloat16*>(k_out);
+  a.q_in_stride = q_in_stride;
+  a.q_out_stride = q_out_stride;
+  a.k_in_stride = k_in_stride;
+  a.k_out_stride = k_out_stride;
+  a.cos_sin = cos_sin_cache;
+  a.max_position = max_position;
+  a.n_tokens = n_tokens;
+  a.Hq = num_heads;
+  a.Hkv = num_kv_heads;
+  a.err = err_flag;
+  cudaError_t e = dllm::launch_rope(a, num_sms_of_current_device(), reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return DLLM_OK;
 }
 
 int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,

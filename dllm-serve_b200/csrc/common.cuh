@@ -23,6 +23,7 @@ enum DeviceError : int32_t {
   kDevSlotOutOfRange = 1,     // a slot index >= num_slots (write skipped)
   kDevWaitTimeout = 2,        // an mbarrier wait exceeded its time limit
   kDevBadSequence = 3,        // inconsistent per-sequence metadata
+  kDevPositionOutOfRange = 4, // a rotary position outside the cos/sin cache (row zeroed)
 };
 
 DLLM_DEVICE void set_error(int32_t* err, int32_t code) {

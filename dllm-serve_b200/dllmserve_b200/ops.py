@@ -250,6 +250,52 @@ def varlen_attention(
 # ---------------------------------------------------------------------------
 # Scoring + top-k + gather + store (attention.py:308-342, 344-413, 204-233)
 # ---------------------------------------------------------------------------
+def rope_neox(
+    positions: torch.Tensor,
+    query: torch.Tensor,
+    key: torch.Tensor,
+    cos_sin_cache: torch.Tensor,
+    *,
+    query_out: torch.Tensor | None = None,
+    key_out: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """NeoX rotary embedding of ``query`` [N, Hq, 128] and ``key`` [N, Hkv, 128]
+    (bf16) at ``positions`` (int64 [N]) from the fp32 ``cos_sin_cache``
+    [max_position, 128] (cos | sin), as RotaryEmbedding.forward
+    (rotary_embedding.py:41-57). Writes ``query_out``/``key_out`` (new tensors
+    by default; pass the inputs for in place) and returns them."""
+    Hq, D = query.shape[1], query.shape[2]
+    Hkv = key.shape[1]
+    _check_rows("query", query, Hq, D)
+    _check_rows("key", key, Hkv, D)
+    dev = _require_cuda(positions, query, key, cos_sin_cache)
+    if positions.dtype != torch.int64 or not positions.is_contiguous() or positions.numel() != query.shape[0]:
+        raise ValueError("positions must be contiguous int64 [num_tokens]")
+    if key.shape[0] != query.shape[0]:
+        raise ValueError("query and key have different token counts")
+    if (cos_sin_cache.dtype != torch.float32 or cos_sin_cache.dim() != 2 or cos_sin_cache.shape[1] != D
+            or not cos_sin_cache.is_contiguous()):
+        raise ValueError("cos_sin_cache must be contiguous float32 [max_position, head_dim]")
+    if query_out is None:
+        query_out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    if key_out is None:
+        key_out = torch.empty(key.shape, dtype=key.dtype, device=key.device)
+    _check_rows("query_out", query_out, Hq, D)
+    _check_rows("key_out", key_out, Hkv, D)
+    lib = _native.lib()
+    with torch.cuda.device(dev):
+        rc = lib.dllm_rope_neox(
+            positions.data_ptr(), query.data_ptr(), query.stride(0), query_out.data_ptr(),
+            query_out.stride(0), key.data_ptr(), key.stride(0), key_out.data_ptr(), key_out.stride(0),
+            cos_sin_cache.data_ptr(), cos_sin_cache.shape[0], query.shape[0], Hq, Hkv, D,
+            _status_ptr(dev), _stream_ptr(),
+        )
+    _native.check(rc, "rope_neox")
+    if query.shape[0] > 0:
+        LAUNCHES[0] += 1
+    return query_out, key_out
+
+
 def select_kv_store(
     q: torch.Tensor,
     k: torch.Tensor,

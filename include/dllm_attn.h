@@ -14,6 +14,9 @@
  *   dllm_attn_varlen_paged_fwd
  *                             <- the same with the cached rows read from the paged cache by
  *                                slot (load_kvcache fused in, attention.py:241-263)
+ *   dllm_rope_neox            <- RotaryEmbedding.forward / apply_rotary_emb
+ *                                (dllmserve/layers/rotary_embedding.py:6-16, 41-57), the
+ *                                op the decoder layers apply to q, k just before attention
  *   dllm_select_kv_store      <- _select_important_head_kv (attention.py:344-413) or
  *                                _select_important_kv (attention.py:308-342), followed by
  *                                the k_prefix_suffix[idx] gather and store_kvcache of the
@@ -70,6 +73,7 @@ extern "C" {
 #define DLLM_DEV_SLOT_OUT_OF_RANGE 1
 #define DLLM_DEV_WAIT_TIMEOUT 2
 #define DLLM_DEV_BAD_SEQUENCE 3
+#define DLLM_DEV_POSITION_OUT_OF_RANGE 4
 
 /* Library version (major*10000 + minor*100 + patch). */
 DLLM_API int dllm_version(void);
@@ -175,6 +179,24 @@ DLLM_API int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, con
                                int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
                                int num_kv_heads, int head_dim, float softmax_scale,
                                int32_t* sched_workspace, int32_t* err_flag, void* stream);
+
+/*
+ * NeoX rotary embedding of q and k (RotaryEmbedding.forward, rotary_embedding.py:41-57,
+ * with apply_rotary_emb :6-16): for token t at position p = positions[t], every head row
+ * x (head_dim 128, bf16) becomes [x1*cos - x2*sin, x2*cos + x1*sin] where x1, x2 are its
+ * halves in fp32 and cos, sin the halves of cos_sin_cache[p] (fp32 [max_position, 128],
+ * cos | sin, as the reference builds it). Products and sums are rounded separately, so
+ * the result equals the reference's bit for bit. q_in/q_out: [n_tokens, num_heads, 128],
+ * k_in/k_out: [n_tokens, num_kv_heads, 128], token strides in elements (multiples of 8);
+ * out may equal in (in place). Positions outside [0, max_position) give zero rows and
+ * flag DLLM_DEV_POSITION_OUT_OF_RANGE.
+ */
+DLLM_API int dllm_rope_neox(const int64_t* positions, const void* q_in, int64_t q_in_stride,
+                            void* q_out, int64_t q_out_stride, const void* k_in,
+                            int64_t k_in_stride, void* k_out, int64_t k_out_stride,
+                            const float* cos_sin_cache, int64_t max_position, int64_t n_tokens,
+                            int num_heads, int num_kv_heads, int head_dim, int32_t* err_flag,
+                            void* stream);
 
 /*
  * Per-sequence descriptor for dllm_select_kv_store: 8 int32 values per sequence.

@@ -29,18 +29,31 @@ def _fake_reference(name):
     utils.__path__ = []
     ctx = types.ModuleType(f"{name}.utils.context")
     ctx.get_context = lambda: "ref-context"
+    rope = types.ModuleType(f"{name}.layers.rotary_embedding")
+
+    class RefRotary:
+        pass
+
+    def ref_get_rope(*a, **kw):
+        return "ref-rope"
+
+    RefRotary.__module__ = ref_get_rope.__module__ = rope.__name__
+    rope.RotaryEmbedding = RefRotary
+    rope.get_rope = ref_get_rope
     models = types.ModuleType(f"{name}.models")
     models.__path__ = []
     llada = types.ModuleType(f"{name}.models.llada")
     llada.Attention = RefAttention
+    llada.get_rope = ref_get_rope
     mods = {name: pkg, f"{name}.layers": layers, attn.__name__: attn, f"{name}.utils": utils,
-            ctx.__name__: ctx, f"{name}.models": models, llada.__name__: llada}
+            ctx.__name__: ctx, f"{name}.models": models, llada.__name__: llada, rope.__name__: rope}
     return mods, RefAttention
 
 
 def test_install_patches_reference_modules(monkeypatch):
     from dllmserve_b200 import integration
     from dllmserve_b200.layers import attention as ours
+    from dllmserve_b200.layers import rotary_embedding as our_rope
 
     mods, RefAttention = _fake_reference("fakeref")
     for k, v in mods.items():
@@ -51,11 +64,15 @@ def test_install_patches_reference_modules(monkeypatch):
         assert mods["fakeref.models.llada"].Attention is ours.Attention
         assert mods["fakeref.layers.attention"].store_kvcache is ours.store_kvcache
         assert ours.get_context() == "ref-context"
+        assert mods["fakeref.layers.rotary_embedding"].RotaryEmbedding is our_rope.RotaryEmbedding
+        assert mods["fakeref.layers.rotary_embedding"].get_rope is our_rope.get_rope
+        assert mods["fakeref.models.llada"].get_rope is our_rope.get_rope
         assert "fakeref.models.llada" in patched
     finally:
         integration.uninstall()
     assert mods["fakeref.layers.attention"].Attention is RefAttention
     assert mods["fakeref.models.llada"].Attention is RefAttention
+    assert mods["fakeref.models.llada"].get_rope() == "ref-rope"
     assert ours.get_context() != "ref-context"
 
 
