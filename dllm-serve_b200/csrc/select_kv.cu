@@ -6,16 +6,21 @@
 // followed by the gather of the selected candidate rows and store_kvcache
 // into the sequence's slots (attention.py:204-233).
 //
-// One CTA per (sequence, KV head) with head_select, one CTA per sequence
-// otherwise. The pass over the candidate keys is HBM-bound (one read of each
+// One CTA per (sequence, KV head) with head_select; without it a cluster of
+// kClusterCtas CTAs per sequence that exchange scores and the selection
+// through distributed shared memory (no multicast copies). The pass over the candidate keys is HBM-bound (one read of each
 // candidate row, several rows in flight per half warp). Ranking runs in shared
 // memory: a radix select (4 passes of 8 bits) finds the n_keep-th largest
 // pooled score T, the keys above T plus the lowest-index keys equal to T are
 // compacted, and only those n_keep keys are bitonic-sorted as 64-bit
 // (order-preserving score bits << 32) | (0xffffffff - candidate), so the result
 // is "descending score, ties by ascending candidate index".
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "select_kv.h"
+
+namespace cg = cooperative_groups;
 
 namespace dllm {
 
@@ -25,7 +30,11 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kD = 128;
 constexpr int kRowsInFlight = 4;                     // candidate rows per half warp per pass
-constexpr int kFullSortMax = 2048;  // up to this many (padded) keys a full sort beats radix select
+constexpr int kFullSortMax = 2048;
+// Shared ranking (head_select off) runs as a cluster of kClusterCtas CTAs per
+// sequence: all score a slice of the candidates into the leader's shared
+// memory, the leader selects, all gather a slice of the selected rows.
+constexpr int kClusterCtas = 8;  // up to this many (padded) keys a full sort beats radix select
 
 DLLM_DEVICE uint32_t order_bits(float f) {
   uint32_t u = __float_as_uint(f);
@@ -65,7 +74,9 @@ template <bool kHeadSelect>
 __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int seq = blockIdx.y;
-  const int h = blockIdx.x;  // KV head (head_select) or 0
+  const int h = kHeadSelect ? blockIdx.x : 0;  // KV head (head_select)
+  // shared ranking: rank in the sequence's cluster (0 = leader)
+  const int crank = kHeadSelect ? 0 : (int)cg::this_cluster().block_rank();
   const int* d = a.seq_desc + seq * 8;
   const int tok_start = d[0], L = d[1], blk_start = d[2], blk_len = d[3];
   const int n_keep = d[4], slot_off = d[5], idx_off = d[6], pool_k = d[7];
@@ -91,6 +102,13 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   uint32_t* hist = reinterpret_cast<uint32_t*>(sel + p2max);
   uint32_t* wsum = hist + 256;
   uint32_t* misc = wsum + kWarps;
+  // the leader's scores / selection (distributed shared memory) for the shared path
+  float* lead_scores = scores;
+  const uint64_t* lead_sel = sel;
+  if (!kHeadSelect) {
+    lead_scores = cg::this_cluster().map_shared_rank(scores, 0);
+    lead_sel = cg::this_cluster().map_shared_rank(sel, 0);
+  }
 
   // 1) q_avg = mean over the block's query rows (fp32), attention.py:367 / :315.
   const int qh0 = kHeadSelect ? h * a.group : 0;
@@ -110,7 +128,11 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     q_avg[e] = s / (float)blk_len;
   }
   if (threadIdx.x == 0) misc[2] = 0;  // selection counter
-  __syncthreads();
+  if (kHeadSelect) {
+    __syncthreads();
+  } else {
+    cg::this_cluster().sync();  // every CTA of the cluster runs before any remote access
+  }
 
   // 2) scores, attention.py:374-384 / :317-326.
   if (kHeadSelect) {
@@ -164,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     const int Hkv = a.Hkv, G = a.group;
     const int row_vec = Hkv * kD / 8;  // uint4 (8 bf16) per lane step
     constexpr int kVecBatch = 8;
-    for (int c = warp; c < Klen; c += kWarps) {
+    for (int c = crank * kWarps + warp; c < Klen; c += kClusterCtas * kWarps) {
       const int tok = tok_start + cand_token(c, blk_start, blk_len);
       const uint4* kr = reinterpret_cast<const uint4*>(a.k + (int64_t)tok * a.k_tok_stride);
       float p = 0.f;
@@ -190,10 +212,15 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
         }
       }
       p = warp_sum(p);
-      if (lane == 0) scores[c] = __fdiv_rn(p, a.sqrt_d);
+      if (lane == 0) lead_scores[c] = __fdiv_rn(p, a.sqrt_d);
     }
   }
-  __syncthreads();
+  if (kHeadSelect) {
+    __syncthreads();
+  } else {
+    cg::this_cluster().sync();  // every score is in the leader's shared memory
+  }
+  if (kHeadSelect || crank == 0) {
 
   // 3) max_pool1d(kernel=pool_k, stride 1, padding pool_k/2)[:Klen]
   //    (attention.py:386-393 / :328-335), evaluated where it is read, as
@@ -318,8 +345,11 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     }
   }
 
+  }  // selection (every CTA with head_select, the leader otherwise)
+  if (!kHeadSelect) cg::this_cluster().sync();  // the leader's selection is final
+
   // 7) indices out + gather/store of the selected rows (attention.py:405-411, :222-233).
-  for (int j = threadIdx.x; j < n_keep && a.top_idx != nullptr; j += kThreads) {
+  for (int j = threadIdx.x; j < n_keep && a.top_idx != nullptr && crank == 0; j += kThreads) {
     const int c = (int)(0xffffffffu - (uint32_t)(sel[j] & 0xffffffffu));
     const int64_t o = kHeadSelect ? (int64_t)idx_off + (int64_t)h * n_keep + j : (int64_t)idx_off + j;
     a.top_idx[o] = c;
@@ -357,8 +387,8 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     }
   } else {
     const int row_vec = a.Hkv * kD / 8;  // uint4 per row
-    for (int j = warp; j < n_keep; j += kWarps) {
-      const int c = (int)(0xffffffffu - (uint32_t)(sel[j] & 0xffffffffu));
+    for (int j = crank * kWarps + warp; j < n_keep; j += kClusterCtas * kWarps) {
+      const int c = (int)(0xffffffffu - (uint32_t)(lead_sel[j] & 0xffffffffu));
       const int64_t slot = a.slots[slot_off + j];
       if (slot < 0) continue;
       if (slot >= a.num_slots) {
@@ -377,6 +407,8 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
       }
     }
   }
+  // the leader's shared memory must outlive the other CTAs' reads of it
+  if (!kHeadSelect) cg::this_cluster().sync();
 }
 
 }  // namespace
@@ -392,7 +424,7 @@ cudaError_t launch_select_kv(const SelectArgs& a, bool head_select, int n_seqs, 
   if (n_seqs == 0) return cudaSuccess;
   const int nq = head_select ? a.group : a.Hq;
   const size_t smem = select_kv_smem_bytes(nq, a.max_klen);
-  dim3 grid(head_select ? a.Hkv : 1, n_seqs);
+  dim3 grid(head_select ? a.Hkv : kClusterCtas, n_seqs);
   // The dynamic-smem opt-in is per device and kernel; raise it only when a
   // launch needs more than before (so steady-state launches, including ones
   // recorded into a CUDA graph, make no attribute calls).
@@ -409,11 +441,23 @@ cudaError_t launch_select_kv(const SelectArgs& a, bool head_select, int n_seqs, 
     if (e != cudaSuccess) return e;
     if (have != nullptr) *have = smem;
   }
-  if (head_select)
+  if (head_select) {
     select_kv_kernel<true><<<grid, kThreads, smem, stream>>>(a);
-  else
-    select_kv_kernel<false><<<grid, kThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, select_kv_kernel<false>, a);
 }
 
 }  // namespace dllm
