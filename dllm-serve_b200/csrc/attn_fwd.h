@@ -33,6 +33,10 @@ struct AttnKernelArgs {
   // zero again when the kernel exits. Launches that may run at the same time
   // need distinct workspaces. Null: static round-robin unit order.
   int32_t* sched;
+  // Split kernel: query heads packed into one 128-row tile (GQA, every query
+  // segment <= 128 / qpack rows; the Q tensor map's box is then (64, qpack,
+  // 128 / qpack)). 1: one head per tile. The pair kernel requires 1.
+  int qpack;
   int qunits;              // query units per (sequence, head): 256-row tile pairs (pair
                            // kernel) or 128-row tiles (split kernel); set by the launcher
   int total_units;         // B * Hq * qunits; set by the launcher

@@ -11,7 +11,8 @@
 // cached rows followed by the block's fresh rows (attention.py:235-265).
 //
 // Persistent kernel: one CTA per SM loops over work units = (sequence b,
-// query head h, 128-row query tile). Roles inside the CTA (11 warps):
+// query head h, 128-row query tile), or, for GQA with short query segments,
+// (sequence b, KV head, up to 128/Lq query heads of its group packed in one tile). Roles inside the CTA (11 warps):
 //   warps 0-3  softmax warpgroup 0: kv rows 0-63 of every KV tile
 //   warps 4-7  softmax warpgroup 1: kv rows 64-127 of every KV tile
 //   warp  8    TMA producer: Q tiles (2-deep ring) and the K ring
@@ -182,21 +183,38 @@ DLLM_DEVICE float exp_store_half(const uint32_t (&s)[2][32], float sl2, float m,
 // One work unit: (sequence b, query head hq, 128-row query tile).
 struct Unit {
   bool valid;
-  int hq, hkv;
+  int hq, hkv;     // first query head of the tile, its KV head
+  int nheads;      // query heads packed in the tile (args.qpack mode), else 1
   int q_begin, Lq, q0;
   int k_begin, nk, c_begin, nc, nkv;
 };
 
 // Units are numbered ((b * Hq) + hq) * qunits + t, so consecutive units share
 // a sequence and head (their K/V stay hot in L2 while several CTAs read them).
+// With args.qpack = m > 1 (GQA, every query segment <= 128/m rows) a tile
+// holds the rows of m query heads of one KV group: units ((b * Hkv) + hk) *
+// qunits + c cover heads hk*group + c*m .. + m-1 (qunits = ceil(group / m)).
 DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
   Unit r;
-  const int per_b = a.Hq * a.qunits;
-  const int b = u / per_b;
-  const int rem = u - b * per_b;
-  r.hq = rem / a.qunits;
-  const int t = rem - r.hq * a.qunits;
-  r.hkv = r.hq / a.group;
+  int b, t;
+  if (a.qpack > 1) {
+    const int per_b = a.Hkv * a.qunits;
+    b = u / per_b;
+    const int rem = u - b * per_b;
+    r.hkv = rem / a.qunits;
+    const int c = rem - r.hkv * a.qunits;
+    r.hq = r.hkv * a.group + c * a.qpack;
+    r.nheads = min(a.qpack, a.group - c * a.qpack);
+    t = 0;
+  } else {
+    const int per_b = a.Hq * a.qunits;
+    b = u / per_b;
+    const int rem = u - b * per_b;
+    r.hq = rem / a.qunits;
+    t = rem - r.hq * a.qunits;
+    r.hkv = r.hq / a.group;
+    r.nheads = 1;
+  }
   r.q_begin = a.cu_q[b];
   r.Lq = a.cu_q[b + 1] - r.q_begin;
   r.q0 = t * kTileM;
@@ -598,10 +616,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // Epilogue: merge the two halves, O / l -> bf16 -> global. Warpgroup w
       // writes output columns [64w, 64w + 64).
-      const int row = t.q0 + row_in_tile;
-      const bool row_ok = row < t.Lq;
+      // tile row -> (query row, packed head): the TMA box stores row r of head
+      // hq + hh at tile row r * qpack + hh
+      const int rr = row_in_tile / args.qpack;
+      const int hh = row_in_tile - rr * args.qpack;
+      const int row = t.q0 + rr;
+      const bool row_ok = row < t.Lq && hh < t.nheads;
       __nv_bfloat16* orow = args.o + (int64_t)(t.q_begin + row) * args.o_tok_stride +
-                            (int64_t)t.hq * args.o_head_stride + wg * kHalfN;
+                            (int64_t)(t.hq + hh) * args.o_head_stride + wg * kHalfN;
       if (t.nkv > 0) {
         ok = mbar_wait_warp(bar(BAR_OFULL), o_it & 1, abort_flag);
         if (!ok) break;
@@ -701,8 +723,15 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   AttnKernelArgs a = args;
-  a.qunits = (max_q + split::kTileM - 1) / split::kTileM;
-  const long long units = (long long)a.B * a.Hq * a.qunits;
+  long long units;
+  if (a.qpack > 1) {
+    if (max_q > split::kTileM / a.qpack) return cudaErrorInvalidValue;
+    a.qunits = (a.group + a.qpack - 1) / a.qpack;
+    units = (long long)a.B * a.Hkv * a.qunits;
+  } else {
+    a.qunits = (max_q + split::kTileM - 1) / split::kTileM;
+    units = (long long)a.B * a.Hq * a.qunits;
+  }
   if (units == 0) return cudaSuccess;
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_units = (int)units;

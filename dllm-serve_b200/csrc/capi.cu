@@ -65,16 +65,18 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 3-D map over [rows, heads, 128] bf16: dims (d, head, row), box (64, 1,
-// box_rows), 128-byte swizzle (matches the UMMA SW128 K-major / MN-major smem
-// layout). Queries use 128-row boxes, keys/values 64-row boxes.
+// 3-D map over [rows, heads, 128] bf16: dims (d, head, row), box (64,
+// box_heads, box_rows), 128-byte swizzle (matches the UMMA SW128 K-major /
+// MN-major smem layout: the box lands as box_rows * box_heads rows of 128 B,
+// row r of head h at r * box_heads + h). Queries use 128-row boxes (or
+// packed GQA boxes of 128 / m rows x m heads), keys/values 128-row boxes.
 int encode_rows_map(CUtensorMap* m, const void* ptr, int64_t rows, int heads, int64_t tok_stride,
-                    int box_rows) {
+                    int box_rows, int box_heads = 1) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return fail(DLLM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {128, (cuuint64_t)heads, (cuuint64_t)(rows > 0 ? rows : 1)};
   cuuint64_t strides[2] = {128 * 2, (cuuint64_t)tok_stride * 2};
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_heads, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -130,7 +132,18 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   }
   CUtensorMap tq, tk, tv, tkc, tvc;
   const int kv_rows = dllm::attn_fwd_kv_rows_per_tile();
-  if ((rc = encode_rows_map(&tq, q, total_q, Hq, q_tok_stride, 128)) != DLLM_OK) return rc;
+  // GQA launches whose query segments are short (the reuse steps' blocks) pack
+  // m query heads of a KV group into one 128-row tile of the split kernel.
+  int qpack = 1;
+  if (max_q <= dllm::kSplitMaxQ) {
+    for (int m = 4; m >= 2; m >>= 1) {
+      if (Hq / Hkv >= m && max_q <= 128 / m) {
+        qpack = m;
+        break;
+      }
+    }
+  }
+  if ((rc = encode_rows_map(&tq, q, total_q, Hq, q_tok_stride, 128 / qpack, qpack)) != DLLM_OK) return rc;
   if ((rc = encode_rows_map(&tk, k, total_k, Hkv, k_tok_stride, kv_rows)) != DLLM_OK) return rc;
   if ((rc = encode_rows_map(&tv, v, total_k, Hkv, v_tok_stride, kv_rows)) != DLLM_OK) return rc;
   if (cu_c != nullptr && total_c > 0) {
@@ -160,6 +173,7 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.vc = reinterpret_cast<const __nv_bfloat16*>(vc);
   a.c_tok_stride = kc_tok_stride;
   a.sched = sched;
+  a.qpack = qpack;
   a.qunits = 0;
   a.total_units = 0;
   // Query segments that fit one tile (the reuse steps' fresh blocks) go to the
