@@ -754,7 +754,7 @@ def run_sparse_cycle(args):
 
 def run_kernels_case(args):
     """Small profiling case: each native kernel launched 3 times on inputs
-    larger than L2 (one c2 layer for attention and the KV store, config-5
+    larger than L2 (one c2 layer for attention, the KV store and RoPE, config-5
     shapes for scoring/top-k and for the reuse-state attention)."""
     from dllmserve_b200 import _native, ops
 
@@ -775,6 +775,12 @@ def run_kernels_case(args):
     slot = torch.randperm(pages * 256, device=dev, generator=g)[:N].to(torch.int32)
     for _ in range(3):
         ops.store_kvcache(k, v, kc, vc, slot)
+    from dllmserve_b200.layers.rotary_embedding import RotaryEmbedding
+
+    rope = RotaryEmbedding(HEAD_DIM, HEAD_DIM, 4096, 500000.0).to(dev)
+    pos = torch.cat([torch.arange(L, device=dev) for L in lens])
+    for _ in range(3):
+        ops.rope_neox(pos, q, k, rope.cos_sin_cache)
     del q, k, v
     # config 5: B=8, L=4096+512, block 32 at the start of the generation, r=0.25
     B5, L5, blk = 8, 4608, 32
