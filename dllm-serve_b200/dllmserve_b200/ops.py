@@ -160,21 +160,20 @@ def _check_rows(name, t, heads, head_dim):
 _SCHED_WS: dict = {}
 
 
-def sched_workspace(dev: torch.device) -> int:
-    """Device pointer of the attention scheduler workspace of ``dev`` (zeroed
-    int32 words the kernel leaves zero), or 0 (round-robin order) when none
-    exists yet and the current stream is being captured: memory allocated
-    during a capture belongs to that graph and must not be cached. One
-    workspace per device: attention launches of this package on one device
-    are stream-ordered (concurrent launches on several streams would need one
-    workspace each)."""
+def sched_workspace(dev: torch.device, stream: int) -> int:
+    """Device pointer of the attention scheduler workspace of (``dev``,
+    ``stream``): zeroed int32 words that every launch leaves zero. Launches on
+    one stream are ordered, so they can share one; launches on different
+    streams may overlap and get their own. Returns 0 (round-robin order, same
+    results) when the stream has none yet and is being captured: memory
+    allocated during a capture belongs to that graph and must not be cached."""
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    ws = _SCHED_WS.get(idx)
+    ws = _SCHED_WS.get((idx, stream))
     if ws is None:
         if torch.cuda.is_current_stream_capturing():
             return 0
         ws = torch.zeros(_native.SCHED_WORKSPACE_INTS, dtype=torch.int32, device=torch.device("cuda", idx))
-        _SCHED_WS[idx] = ws
+        _SCHED_WS[(idx, stream)] = ws
     return ws.data_ptr()
 
 
@@ -223,7 +222,8 @@ def varlen_attention(
     lib = _native.lib()
     status = _status_ptr(dev)
     with _on_device(dev):
-        sched = sched_workspace(dev)
+        stream = _stream_ptr()
+        sched = sched_workspace(dev, stream)
         if k_cache is not None:
             _require_cuda(q, k_cache, v_cache, slots, cu_seqlens_slots)
             if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
@@ -242,14 +242,14 @@ def varlen_attention(
                 k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row,
                 slots.data_ptr(), cu_seqlens_slots.data_ptr(), out.data_ptr(), out.stride(0),
                 cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), B, int(max_seqlen_q), q.shape[0],
-                k.shape[0], Hq, Hkv, D, float(softmax_scale), sched, status, _stream_ptr(),
+                k.shape[0], Hq, Hkv, D, float(softmax_scale), sched, status, stream,
             )
         elif k_cached is None:
             rc = lib.dllm_attn_varlen_fwd(
                 q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
                 out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
                 B, int(max_seqlen_q), q.shape[0], k.shape[0], Hq, Hkv, D, float(softmax_scale),
-                sched, status, _stream_ptr(),
+                sched, status, stream,
             )
         else:
             _check_rows("k_cached", k_cached, Hkv, D)
@@ -264,7 +264,7 @@ def varlen_attention(
                 k_cached.data_ptr(), k_cached.stride(0), v_cached.data_ptr(), v_cached.stride(0),
                 out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
                 cu_seqlens_c.data_ptr(), B, int(max_seqlen_q), q.shape[0], k.shape[0],
-                k_cached.shape[0], Hq, Hkv, D, float(softmax_scale), sched, status, _stream_ptr(),
+                k_cached.shape[0], Hq, Hkv, D, float(softmax_scale), sched, status, stream,
             )
     _native.check(rc, "varlen_attention")
     if B > 0 and q.shape[0] > 0:

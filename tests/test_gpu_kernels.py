@@ -160,8 +160,8 @@ def test_attention_separate_q_and_k_lengths(dev):
 
 @pytest.mark.parametrize("batch", [256, 300])
 def test_attention_many_sequences(dev, batch):
-    """Batches up to 256 sequences use the cost-ranked unit schedule, larger
-    ones the natural order; empty query or key segments included."""
+    """Hundreds of ragged sequences in one launch (short ones: the split
+    kernel), with empty query or key segments."""
     g = I.gen(90 + batch)
     D, hq, hkv = 128, 2, 1
     lq = torch.randint(0, 300, (batch,), generator=g).tolist()
@@ -211,6 +211,32 @@ def test_attention_sched_workspace_matches_round_robin(dev):
     assert int(ws.abs().sum()) == 0
     _check_attn(ref, R.varlen_attention(q.float().cpu(), k.float().cpu(), v.float().cpu(),
                                         _cu(lens), _cu(lens), D ** -0.5))
+
+
+def test_attention_two_streams_at_once(dev):
+    """Launches overlapping on two streams use separate scheduler workspaces:
+    both outputs equal the single-stream result bit for bit."""
+    g = I.gen(141)
+    D, H = 128, 8
+    lens = [900, 300, 1087, 129, 640]
+    N = sum(lens)
+    q, k, v = (I.normal(g, (N, H, D)).to(dev, torch.bfloat16) for _ in range(3))
+    cu = torch.tensor(_cu(lens), dtype=torch.int32, device=dev)
+    ops = _ops()
+    ref = ops.varlen_attention(q, k, v, cu, cu, max(lens))
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = []
+    for s in (s1, s2):
+        s.wait_stream(torch.cuda.current_stream())
+    for rep in range(4):
+        for s in (s1, s2):
+            with torch.cuda.stream(s):
+                outs.append(ops.varlen_attention(q, k, v, cu, cu, max(lens)))
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, ref)
+    _status_clear(dev)
 
 
 def test_attention_fused_qkv_views(dev):
