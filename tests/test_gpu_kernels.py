@@ -384,6 +384,10 @@ SEL_CASES = [
     (4, 2, True, 3, 0.0, [(100, 10, 32)]),
     (4, 2, True, 3, 1.0, [(100, 10, 32)]),
     (32, 32, True, 3, 0.25, [(4608, 4096, 32)]),
+    # shared ranking at config-5 size (radix select in the cluster leader) and a
+    # GQA batch of several sequences (one cluster each)
+    (32, 32, False, 3, 0.25, [(4608, 4096, 32)]),
+    (28, 4, False, 3, 0.5, [(704, 448, 32), (300, 100, 32), (2600, 2000, 32)]),
 ]
 
 
