@@ -276,6 +276,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Everything above (barriers, TMEM, descriptor prefetch) may overlap the
+  // previous kernel in the stream; every global access below comes after it.
+  griddep_wait();
+  griddep_launch_dependents();
   volatile int* uring = reinterpret_cast<volatile int*>(smem + kOffRing);
   // consumer side: next unit id from the ring (bounded wait); -1 on abort
   // warp_wide: every lane of the warp calls it (one arrival from lane 0);
@@ -715,8 +719,19 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, cons
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_units = (int)units;
   const int grid = (int)(units < num_sms ? units : num_sms);
-  attn_fwd_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmQ, tmK, tmV, tmKc, tmVc, a);
-  return cudaGetLastError();
+  // Programmatic dependent launch: this grid may start while the previous
+  // kernel in the stream finishes; it waits for it in griddep_wait().
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attn_fwd_kernel, tmQ, tmK, tmV, tmKc, tmVc, a);
 }
 
 }  // namespace dllm

@@ -299,6 +299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Everything above (barriers, TMEM, descriptor prefetch) may overlap the
+  // previous kernel in the stream; every global access below comes after it.
+  griddep_wait();
+  griddep_launch_dependents();
   if (threadIdx.x == 9 * 32) TRACE(1, 0, 0);
 
   if (warp == 8 || warp == 10) {
@@ -736,8 +740,19 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_units = (int)units;
   const int grid = (int)(units < num_sms ? units : num_sms);
-  split::attn_fwd_split_kernel<<<grid, split::kThreads, split::kSmemBytes, stream>>>(tmQ, tmK, tmV, tmKc, tmVc, a);
-  return cudaGetLastError();
+  // Programmatic dependent launch: this grid may start while the previous
+  // kernel in the stream finishes; it waits for it in griddep_wait().
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(split::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = split::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, split::attn_fwd_split_kernel, tmQ, tmK, tmV, tmKc, tmVc, a);
 }
 
 }  // namespace dllm

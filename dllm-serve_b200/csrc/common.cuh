@@ -130,6 +130,12 @@ DLLM_DEVICE void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// Programmatic dependent launch: wait until the grids this one depends on have
+// completed (and their memory is visible); allow the next grid in the stream
+// to start launching (it still waits in its own griddep_wait).
+DLLM_DEVICE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+DLLM_DEVICE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 3-D tiled load, completes tx bytes on `bar`. No multicast.
 DLLM_DEVICE void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1, int c2,
                              uint64_t cache_hint) {
