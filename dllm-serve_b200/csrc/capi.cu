@@ -117,6 +117,7 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   if (batch < 0 || max_q < 0 || total_q < 0 || total_k < 0 || total_c < 0)
     return fail(DLLM_ERR_INVALID_ARG, "negative size");
   if (!(scale > 0.f)) return fail(DLLM_ERR_INVALID_ARG, "softmax_scale must be > 0");
+  if (!aligned(sched, 4)) return fail(DLLM_ERR_ALIGNMENT, "sched_workspace is not 4-byte aligned");
   if (batch == 0 || total_q == 0 || max_q == 0) return DLLM_OK;
   if (cu_q == nullptr || cu_k == nullptr) return fail(DLLM_ERR_INVALID_ARG, "cu_seqlens is null");
   int rc;

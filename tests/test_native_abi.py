@@ -52,6 +52,10 @@ def test_validation_errors_without_gpu():
     rc = lib.dllm_attn_varlen_fwd(None, 0, None, 0, None, 0, None, 0, None, None, 1, 1, 1, 1,
                                   4, 4, 128, ctypes.c_float(0.0), None, None, None)
     assert rc == _native.DLLM_ERR_INVALID_ARG
+    # a misaligned scheduler workspace is refused before any device work
+    rc = lib.dllm_attn_varlen_fwd(None, 0, None, 0, None, 0, None, 0, None, None, 1, 1, 1, 1,
+                                  4, 4, 128, ctypes.c_float(0.1), 2, None, None)
+    assert rc == _native.DLLM_ERR_ALIGNMENT
     # empty batch is a no-op
     rc = lib.dllm_attn_varlen_fwd(None, 0, None, 0, None, 0, None, 0, None, None, 0, 0, 0, 0,
                                   4, 4, 128, ctypes.c_float(0.1), None, None, None)
