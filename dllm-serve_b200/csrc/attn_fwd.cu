@@ -32,6 +32,9 @@ namespace {
 constexpr int kD = 128;          // head dim (only 128 is instantiated)
 constexpr int kTileM = 128;      // query rows per tile
 constexpr int kTileN = 128;      // kv rows per tile
+#ifndef DLLM_EPI_QUAD
+#define DLLM_EPI_QUAD 1  // lane-quad transposed output stores
+#endif
 constexpr int kStagesK = 3;      // K ring depth (K runs one tile ahead of V)
 constexpr int kStagesV = 2;      // V ring depth
 constexpr int kThreads = 352;
@@ -646,6 +649,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_in_tile == 0) TRACE(14, 0, wg);
         tc_fence_after();
         const float inv_l = 1.f / l;
+#if DLLM_EPI_QUAD
+        // Rows are spread one per lane; a 4x4 transpose of 16-byte vectors
+        // inside each lane quad lets every store instruction write 8 rows x 64
+        // contiguous bytes (full sectors) instead of 32 rows x 16 bytes.
+        const int qj = lane & 3;
+        const int qrow0 = row - qj;  // first row of this lane's quad
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+          uint4 v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            v[e].x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv_l, __uint_as_float(o[8 * e + 1]) * inv_l);
+            v[e].y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv_l, __uint_as_float(o[8 * e + 3]) * inv_l);
+            v[e].z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv_l, __uint_as_float(o[8 * e + 5]) * inv_l);
+            v[e].w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv_l, __uint_as_float(o[8 * e + 7]) * inv_l);
+          }
+          quad_transpose16(v, qj);  // v[r] = vector qj of the quad's row r
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            if (qrow0 + r < t.Lq) {
+              uint4* dst = reinterpret_cast<uint4*>(orow + (int64_t)(r - qj) * args.o_tok_stride + c * 32);
+              dst[qj] = v[r];
+            }
+          }
+        }
+#else
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -664,6 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+#endif
         // O_i is read out; the next unit's first PV may overwrite it once this
         // warpgroup arrives on its first P barrier (program order + fence).
         tc_fence_before();

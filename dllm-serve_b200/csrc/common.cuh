@@ -299,6 +299,33 @@ DLLM_DEVICE float max3f(float a, float b, float c) {
   return d;
 }
 
+// 4x4 transpose of 16-byte vectors inside each quad of lanes (j = lane & 3):
+// on return v[r] holds what lane r of the quad had in v[j]. Two butterfly
+// stages (xor 2 swaps the off-diagonal 2x2 blocks, xor 1 the off-diagonal
+// elements inside them); every lane of the warp must take part.
+DLLM_DEVICE uint4 shfl_xor_u4(uint4 a, int m) {
+  uint4 r;
+  r.x = __shfl_xor_sync(0xffffffffu, a.x, m);
+  r.y = __shfl_xor_sync(0xffffffffu, a.y, m);
+  r.z = __shfl_xor_sync(0xffffffffu, a.z, m);
+  r.w = __shfl_xor_sync(0xffffffffu, a.w, m);
+  return r;
+}
+DLLM_DEVICE void quad_transpose16(uint4 (&v)[4], int j) {
+  const bool hi = (j & 2) != 0;
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const uint4 r = shfl_xor_u4(hi ? v[s] : v[2 + s], 2);
+    if (hi) v[s] = r; else v[2 + s] = r;
+  }
+  const bool odd = (j & 1) != 0;
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const uint4 r = shfl_xor_u4(odd ? v[2 * s] : v[2 * s + 1], 1);
+    if (odd) v[2 * s] = r; else v[2 * s + 1] = r;
+  }
+}
+
 DLLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
