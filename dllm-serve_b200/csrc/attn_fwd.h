@@ -40,6 +40,13 @@ struct AttnKernelArgs {
   int qunits;              // query units per (sequence, head): 256-row tile pairs (pair
                            // kernel) or 128-row tiles (split kernel); set by the launcher
   int total_units;         // B * Hq * qunits; set by the launcher
+  // Rotary embedding applied on chip (split kernel only; null positions: off).
+  // Query row r and fresh key row r are rotated by cos_sin[positions[r]]
+  // between their TMA arrival and the MMA that reads them; cached rows are
+  // taken as already rotated.
+  const int64_t* positions;
+  const float* cos_sin;    // [max_position, 128] fp32: cos | sin halves
+  int64_t max_position;
 };
 
 uint32_t attn_fwd_smem_bytes();

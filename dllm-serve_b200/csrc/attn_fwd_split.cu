@@ -18,6 +18,8 @@
 //   warp  8    TMA producer: Q tiles (2-deep ring) and the K ring
 //   warp  9    MMA issuer (also allocates / frees TMEM)
 //   warp  10   TMA producer: the V ring
+//   warp  11   (rotary launches only) rotates each Q tile and each fresh K
+//              tile in shared memory between its TMA arrival and its MMA
 // Both warpgroups own all 128 query rows (TMEM lanes) and split each KV
 // tile's 128 columns; each keeps its own running max / sum and its own
 // output accumulator, and the two partial results are merged once per unit.
@@ -50,6 +52,7 @@ constexpr int kStagesQ = 2;      // Q ring depth (the next unit's Q loads early)
 constexpr int kStagesK = 3;      // K ring depth (QK runs two tiles ahead of PV)
 constexpr int kStagesV = 2;      // V ring depth
 constexpr int kThreads = 352;
+constexpr int kThreadsRope = 384;  // + the rotary warp
 
 // Softmax code-shape switch (tuning; default is the measured best).
 #ifndef DLLM_SM_POLY
@@ -79,7 +82,10 @@ constexpr int BAR_OFULL = BAR_OREADY + 1;         // 1: a unit's last PVs comple
 constexpr int BAR_XML = BAR_OFULL + 1;            // 1: warpgroup 1's (max, sum) published
 constexpr int BAR_XF = BAR_XML + 1;               // 1: the merge factors published
 constexpr int BAR_DRAIN = BAR_XF + 1;             // 1
-constexpr uint32_t kNumBars = BAR_DRAIN + 1;
+constexpr int BAR_QROPED = BAR_DRAIN + 1;         // kStagesQ: Q tile rotated (rotary launches)
+constexpr int BAR_KROPED = BAR_QROPED + kStagesQ; // kStagesK: fresh K tile rotated
+constexpr int BAR_KFRESH = BAR_KROPED + kStagesK; // kStagesK: fresh K tile landed (rotary launches)
+constexpr uint32_t kNumBars = BAR_KFRESH + kStagesK;
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;           // abort flag, TMEM address
 constexpr uint32_t kOffXch = kOffMisc + 64;                     // float2 per query row
 constexpr uint32_t kSmemBytes = kOffXch + kTileM * 8 + 1024;    // + alignment slack
@@ -231,11 +237,81 @@ DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
   return r;
 }
 
+// Rotates, in place in shared memory, the rows of one SW128 tile (two 64-column
+// halves kChunkBytes apart, 128-byte lines, 16-byte unit u of line r stored at
+// unit u ^ (r mod 8)): line rr * qpack + hh holds head hh of token tok0 + rr
+// (rr < rows, hh < nheads <= 4; other lines are left alone). Dimension pair
+// (d, d + 64) sits at the same offset of the two halves. One warp: lane l
+// covers unit (l mod 8) of rows l/8 + 4i; the positions, then the cos/sin rows
+// of 16 rows are loaded at once (one round trip each) and applied to every
+// head of the row.
+DLLM_DEVICE void rope_tile_smem(uint8_t* tile, int lane, const AttnKernelArgs& a, int64_t tok0,
+                                int rows, int qpack, int nheads) {
+  const int c = lane & 7;
+  for (int rb = lane >> 3; rb < rows; rb += 16) {
+    int64_t pos[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = rb + 4 * i;
+      pos[i] = r < rows ? __ldg(a.positions + tok0 + r) : 0;
+    }
+    float4 cv[4][2], sv[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = rb + 4 * i;
+      const bool in_range = pos[i] >= 0 && pos[i] < a.max_position;
+      if (r < rows && !in_range) set_error(a.err, kDevPositionOutOfRange);
+      if (r < rows && in_range) {
+        const float4* row = reinterpret_cast<const float4*>(a.cos_sin + pos[i] * kD);
+        cv[i][0] = __ldg(row + 2 * c);
+        cv[i][1] = __ldg(row + 2 * c + 1);
+        sv[i][0] = __ldg(row + 16 + 2 * c);
+        sv[i][1] = __ldg(row + 16 + 2 * c + 1);
+      } else {  // out of range: the row becomes zero
+        cv[i][0] = cv[i][1] = sv[i][0] = sv[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = rb + 4 * i;
+      if (r >= rows) continue;
+      // Scalar fp32 products and sums: the packed f32x2 forms of the same
+      // operations were measured to differ from them in the last bf16 bit of
+      // a few outputs, so they are not used here.
+      const float cs[8] = {cv[i][0].x, cv[i][0].y, cv[i][0].z, cv[i][0].w,
+                           cv[i][1].x, cv[i][1].y, cv[i][1].z, cv[i][1].w};
+      const float sn[8] = {sv[i][0].x, sv[i][0].y, sv[i][0].z, sv[i][0].w,
+                           sv[i][1].x, sv[i][1].y, sv[i][1].z, sv[i][1].w};
+      uint4 w[4][2];
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) {
+        if (hh < nheads) {
+          const int line = r * qpack + hh;
+          const uint32_t off = line * 128 + ((c ^ (line & 7)) << 4);
+          w[hh][0] = *reinterpret_cast<const uint4*>(tile + off);
+          w[hh][1] = *reinterpret_cast<const uint4*>(tile + kChunkBytes + off);
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) {
+        if (hh < nheads) {
+          const int line = r * qpack + hh;
+          const uint32_t off = line * 128 + ((c ^ (line & 7)) << 4);
+          rope_rotate8(w[hh][0], w[hh][1], cs, sn);
+          *reinterpret_cast<uint4*>(tile + off) = w[hh][0];
+          *reinterpret_cast<uint4*>(tile + kChunkBytes + off) = w[hh][1];
+        }
+      }
+    }
+  }
+}
+
 // Persistent kernel: CTA c processes units c, c + gridDim.x, ... Barrier
 // phases run on across units (ring counters below), so the producers load the
 // next unit's Q/K/V and the MMA warp starts its QKs while the softmax warps
 // still write the previous unit's output.
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool kRope>
+__global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
     attn_fwd_split_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKc,
                     const __grid_constant__ CUtensorMap tmVc, AttnKernelArgs args) {
@@ -279,6 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(BAR_XML), 128);  // every thread of warpgroup 1
     mbar_init(bar(BAR_XF), 128);   // every thread of warpgroup 0
     mbar_init(bar(BAR_DRAIN), 1);
+    for (int s = 0; s < kStagesQ; ++s) mbar_init(bar(BAR_QROPED + s), 1);
+    for (int s = 0; s < kStagesK; ++s) {
+      mbar_init(bar(BAR_KROPED + s), 1);
+      mbar_init(bar(BAR_KFRESH + s), 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -321,6 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const __nv_bfloat16* cache = kq ? args.kc : args.vc;
     uint32_t q_it = 0;     // units whose Q was loaded (warp 8)
     uint32_t done = 0;     // tiles issued into this ring
+    // Rotary launches, K ring: a fresh tile completes on its stage's KFRESH
+    // barrier instead of KFULL; per-stage phase parities of both barriers and
+    // which of them each stage's latest load used (for the drain).
+    uint32_t kfull_par = 0, kfresh_par = 0, last_fresh = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       const Unit t = decode_unit(u, args);
@@ -393,9 +478,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (lane == 0) {
           const CUtensorMap* mp = kq ? (kt.seg == 0 ? &tmKc : &tmK) : (kt.seg == 0 ? &tmVc : &tmV);
-          mbar_arrive_expect_tx(bar(bfull + st), kTileBytes);
-          tma_load_3d(dk, mp, bar(bfull + st), 0, t.hkv, kt.row0, pol_kv);
-          tma_load_3d(dk + kChunkBytes, mp, bar(bfull + st), 64, t.hkv, kt.row0, pol_kv);
+          const uint32_t fb = bar(((kRope && kq && kt.seg == 1) ? BAR_KFRESH : bfull) + st);
+          mbar_arrive_expect_tx(fb, kTileBytes);
+          tma_load_3d(dk, mp, fb, 0, t.hkv, kt.row0, pol_kv);
+          tma_load_3d(dk + kChunkBytes, mp, fb, 64, t.hkv, kt.row0, pol_kv);
+        }
+        if (kRope && kq) {
+          const uint32_t bit = 1u << st;
+          if (kt.seg == 1) {
+            kfresh_par ^= bit;
+            last_fresh |= bit;
+          } else {
+            kfull_par ^= bit;
+            last_fresh &= ~bit;
+          }
         }
         ++done;
         if (lane == 0) TRACE(kq ? 2 : 3, j, 0);
@@ -406,8 +502,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (kq)
         for (uint32_t n = (q_it > (uint32_t)kStagesQ ? q_it - kStagesQ : 0); n < q_it; ++n)
           mbar_wait_drain(bar(BAR_QFULL + n % kStagesQ), (n / kStagesQ) & 1, 100000000ull);
-      for (uint32_t n = (done > (uint32_t)nst ? done - nst : 0); n < done; ++n)
-        mbar_wait_drain(bar(bfull + n % nst), (n / nst) & 1, 100000000ull);
+      if (kRope && kq) {
+        // the latest load of each stage, on the barrier it completes on
+        for (int st = 0; st < nst && st < (int)done; ++st) {
+          const uint32_t bit = 1u << st;
+          if (last_fresh & bit)
+            mbar_wait_drain(bar(BAR_KFRESH + st), ((kfresh_par & bit) ? 1u : 0u) ^ 1u, 100000000ull);
+          else
+            mbar_wait_drain(bar(BAR_KFULL + st), ((kfull_par & bit) ? 1u : 0u) ^ 1u, 100000000ull);
+        }
+      } else {
+        for (uint32_t n = (done > (uint32_t)nst ? done - nst : 0); n < done; ++n)
+          mbar_wait_drain(bar(bfull + n % nst), (n / nst) & 1, 100000000ull);
+      }
     }
     __syncwarp();
   } else if (warp == 9) {
@@ -454,12 +561,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       uint32_t q_it = 0, k_it = 0, v_it = 0;
       uint32_t g = 0;  // KV tiles whose PVs were issued (all units), = S tile index
+      // Rotary launches: per-stage phase parities of KFULL (cached tiles) and
+      // KROPED (fresh tiles, released by the rotary warp).
+      uint32_t kc_par = 0, kr_par = 0;
+      // A K tile is ready for QK once it landed, or, for a fresh tile of a
+      // rotary launch, once the rotary warp released it.
+      auto wait_k = [&](int kst, int seg) -> bool {
+        if (kRope) {
+          uint32_t& pp = seg == 1 ? kr_par : kc_par;
+          const uint32_t par = (pp >> kst) & 1u;
+          pp ^= 1u << kst;
+          return mbar_wait(bar((seg == 1 ? BAR_KROPED : BAR_KFULL) + kst), par, abort_flag);
+        }
+        return mbar_wait(bar(BAR_KFULL + kst), (k_it / kStagesK) & 1, abort_flag);
+      };
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
         const Unit t = decode_unit(u, args);
         if (!t.valid) continue;
         const int qs = q_it % kStagesQ;
-        ok = mbar_wait(bar(BAR_QFULL + qs), (q_it / kStagesQ) & 1, abort_flag);
+        ok = mbar_wait(bar((kRope ? BAR_QROPED : BAR_QFULL) + qs), (q_it / kStagesQ) & 1, abort_flag);
         if (!ok) break;
         ++q_it;
         if (t.nkv == 0) {
@@ -471,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < npro && ok; ++j) {
           const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
           const int kst = k_it % kStagesK;
-          ok = mbar_wait(bar(BAR_KFULL + kst), (k_it / kStagesK) & 1, abort_flag);
+          ok = wait_k(kst, kt.seg);
           if (!ok) break;
           tc_fence_after();
           qk(qs, kst, kt.valid, (g + j) & 1);
@@ -504,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j + 2 < t.nkv) {
             const KvTile kn = kv_tile(j + 2, t.nc, t.c_begin, t.nk, t.k_begin);
             const int kst = k_it % kStagesK;
-            ok = mbar_wait(bar(BAR_KFULL + kst), (k_it / kStagesK) & 1, abort_flag);
+            ok = wait_k(kst, kn.seg);
             if (!ok) break;
             tc_fence_after();
             qk(qs, kst, kn.valid, sb);  // tile g + 2 uses the same S buffer
@@ -521,6 +642,90 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Make sure every issued MMA has finished before TMEM is released.
       umma_commit(bar(BAR_DRAIN));
       mbar_wait_drain(bar(BAR_DRAIN), 0, 100000000ull);
+    }
+    __syncwarp();
+  } else if (warp == 11) {
+    // ------------------------------------------------------------- rotary
+    // (rotary launches only) Two independent in-order streams, polled: the Q
+    // loads (each rotated and released on its stage's QROPED barrier) and the
+    // fresh K loads (each completes on its stage's KFRESH barrier and is
+    // rotated and released on KROPED). A stage holding a Q tile or a fresh K
+    // tile is refilled only after the MMA warp consumed it, which needs this
+    // warp's release, so neither barrier can run two phases ahead of this
+    // warp. Cached K tiles were rotated before they were stored; they bypass
+    // this warp (only counted, for the ring positions). Polling both streams
+    // lets the next unit's Q be rotated as soon as it lands.
+    int uq = blockIdx.x, uk = blockIdx.x, jk = 0;
+    uint32_t q_it = 0, k_it = 0, kf_par = 0;
+    Unit tq{}, tk{};
+    KvTile kcur{};
+    auto next_q = [&]() {
+      for (; uq < total_units; uq += gridDim.x) {
+        tq = decode_unit(uq, args);
+        if (tq.valid) return true;
+      }
+      return false;
+    };
+    // Moves the K cursor (uk, jk, k_it) to the next fresh tile at or after it.
+    bool k_in_unit = false;
+    auto next_fresh_k = [&]() {
+      while (true) {
+        if (!k_in_unit) {
+          for (; uk < total_units; uk += gridDim.x) {
+            tk = decode_unit(uk, args);
+            if (tk.valid && tk.nkv > 0) break;
+          }
+          if (uk >= total_units) return false;
+          k_in_unit = true;
+          jk = 0;
+        }
+        for (; jk < tk.nkv; ++jk, ++k_it) {
+          kcur = kv_tile(jk, tk.nc, tk.c_begin, tk.nk, tk.k_begin);
+          if (kcur.seg == 1) return true;
+        }
+        k_in_unit = false;
+        uk += gridDim.x;
+      }
+    };
+    bool q_more = next_q(), k_more = next_fresh_k();
+    uint64_t t_last = globaltimer_ns();
+    while ((q_more || k_more) && !*abort_flag) {
+      bool progressed = false;
+      if (k_more) {
+        const int kst = k_it % kStagesK;
+        const uint32_t bit = 1u << kst;
+        if (__all_sync(0xffffffffu, mbar_test_wait(bar(BAR_KFRESH + kst), (kf_par & bit) ? 1u : 0u))) {
+          rope_tile_smem(smem + kOffK + kst * kTileBytes, lane, args, kcur.row0, kcur.valid, 1, 1);
+          fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(BAR_KROPED + kst));
+          kf_par ^= bit;
+          ++jk;
+          ++k_it;
+          k_more = next_fresh_k();
+          progressed = true;
+        }
+      }
+      if (q_more) {
+        const int qs = q_it % kStagesQ;
+        if (__all_sync(0xffffffffu, mbar_test_wait(bar(BAR_QFULL + qs), (q_it / kStagesQ) & 1))) {
+          rope_tile_smem(smem + kOffQ + qs * kTileBytes, lane, args, (int64_t)tq.q_begin + tq.q0,
+                         min(tq.Lq - tq.q0, kTileM / args.qpack), args.qpack, tq.nheads);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(BAR_QROPED + qs));
+          ++q_it;
+          uq += gridDim.x;
+          q_more = next_q();
+          progressed = true;
+        }
+      }
+      if (progressed) {
+        t_last = globaltimer_ns();
+      } else {
+        __nanosleep(64);
+        if (globaltimer_ns() - t_last > kWaitLimitNs) *abort_flag = 1;
+      }
     }
     __syncwarp();
   } else {
@@ -715,16 +920,19 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
                             const CUtensorMap& tmKc, const CUtensorMap& tmVc,
                             const AttnKernelArgs& args, int max_q, int num_sms,
                             cudaStream_t stream) {
-  // The smem opt-in is per device; remember it for up to 64 devices.
-  static bool attr_set[64] = {false};
+  // The smem opt-in is per device and instantiation; remember it for up to 64 devices.
+  static bool attr_set[2][64] = {{false}};
+  const bool rope = args.positions != nullptr;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    e = cudaFuncSetAttribute(split::attn_fwd_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)split::kSmemBytes);
+  if (dev < 0 || dev >= 64 || !attr_set[rope][dev]) {
+    e = rope ? cudaFuncSetAttribute(split::attn_fwd_split_kernel<true>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemBytes)
+             : cudaFuncSetAttribute(split::attn_fwd_split_kernel<false>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)split::kSmemBytes);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[rope][dev] = true;
   }
   AttnKernelArgs a = args;
   long long units;
@@ -744,7 +952,7 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
   // kernel in the stream finishes; it waits for it in griddep_wait().
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(split::kThreads, 1, 1);
+  cfg.blockDim = dim3(rope ? split::kThreadsRope : split::kThreads, 1, 1);
   cfg.dynamicSmemBytes = split::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -752,7 +960,8 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, split::attn_fwd_split_kernel, tmQ, tmK, tmV, tmKc, tmVc, a);
+  return rope ? cudaLaunchKernelEx(&cfg, split::attn_fwd_split_kernel<true>, tmQ, tmK, tmV, tmKc, tmVc, a)
+              : cudaLaunchKernelEx(&cfg, split::attn_fwd_split_kernel<false>, tmQ, tmK, tmV, tmKc, tmVc, a);
 }
 
 }  // namespace dllm

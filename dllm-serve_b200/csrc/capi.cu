@@ -108,7 +108,8 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
                 const int32_t* cu_q, const int32_t* cu_k, const int32_t* cu_c, int batch,
                 int max_q, int64_t total_q, int64_t total_k, int64_t total_c, int Hq, int Hkv,
                 int head_dim, float scale, int32_t* sched, int32_t* err, void* stream,
-                const int32_t* slots = nullptr) {
+                const int32_t* slots = nullptr, const int64_t* positions = nullptr,
+                const float* cos_sin = nullptr, int64_t max_position = 0) {
   if (head_dim != 128)
     return fail(DLLM_ERR_UNSUPPORTED, "head_dim %d not supported (only 128)", head_dim);
   if (Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
@@ -118,6 +119,17 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
     return fail(DLLM_ERR_INVALID_ARG, "negative size");
   if (!(scale > 0.f)) return fail(DLLM_ERR_INVALID_ARG, "softmax_scale must be > 0");
   if (!aligned(sched, 4)) return fail(DLLM_ERR_ALIGNMENT, "sched_workspace is not 4-byte aligned");
+  if (positions != nullptr) {
+    if (cos_sin == nullptr) return fail(DLLM_ERR_INVALID_ARG, "cos_sin_cache is null");
+    if (!aligned(cos_sin, 16)) return fail(DLLM_ERR_ALIGNMENT, "cos_sin_cache must be 16-byte aligned");
+    if (max_position < 0) return fail(DLLM_ERR_INVALID_ARG, "negative size");
+    if (max_q > dllm::kSplitMaxQ)
+      return fail(DLLM_ERR_UNSUPPORTED,
+                  "on-chip rotary needs max_seqlen_q <= %d (got %d); rotate first, then attend",
+                  dllm::kSplitMaxQ, max_q);
+    if (total_q != total_k)
+      return fail(DLLM_ERR_INVALID_ARG, "on-chip rotary needs total_q == total_k (one position per row)");
+  }
   if (batch == 0 || total_q == 0 || max_q == 0) return DLLM_OK;
   if (cu_q == nullptr || cu_k == nullptr) return fail(DLLM_ERR_INVALID_ARG, "cu_seqlens is null");
   int rc;
@@ -177,6 +189,9 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.qpack = qpack;
   a.qunits = 0;
   a.total_units = 0;
+  a.positions = positions;
+  a.cos_sin = cos_sin;
+  a.max_position = max_position;
   // Query segments that fit one tile (the reuse steps' fresh blocks) go to the
   // split kernel, which keeps both softmax warpgroups busy on a lone tile.
   const int sms = num_sms_of_current_device();
@@ -336,6 +351,28 @@ int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, const void* 
                      v_cache, cache_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k,
                      cu_seqlens_slots, batch, max_seqlen_q, total_q, total_k, num_slots, num_heads,
                      num_kv_heads, head_dim, softmax_scale, sched_workspace, err_flag, stream, slots);
+}
+
+int dllm_attn_varlen_rope_fwd(const int64_t* positions, const float* cos_sin_cache,
+                              int64_t max_position, const void* q, int64_t q_tok_stride,
+                              const void* k, int64_t k_tok_stride, const void* v,
+                              int64_t v_tok_stride, const void* k_cache, const void* v_cache,
+                              int64_t cache_tok_stride, int64_t num_slots, const int32_t* slots,
+                              const int32_t* cu_seqlens_slots, void* o, int64_t o_tok_stride,
+                              const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int batch,
+                              int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
+                              int num_kv_heads, int head_dim, float softmax_scale,
+                              int32_t* err_flag, void* stream) {
+  if (positions == nullptr) return fail(DLLM_ERR_INVALID_ARG, "positions is null");
+  if ((slots == nullptr) != (cu_seqlens_slots == nullptr))
+    return fail(DLLM_ERR_INVALID_ARG, "slots and cu_seqlens_slots must both be given or both be null");
+  if (slots != nullptr && num_slots <= 0) return fail(DLLM_ERR_INVALID_ARG, "num_slots must be > 0");
+  return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, k_cache, cache_tok_stride,
+                     v_cache, cache_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k,
+                     cu_seqlens_slots, batch, max_seqlen_q, total_q, total_k,
+                     slots != nullptr ? num_slots : 0, num_heads, num_kv_heads, head_dim,
+                     softmax_scale, nullptr, err_flag, stream, slots, positions, cos_sin_cache,
+                     max_position);
 }
 
 int dllm_rope_neox(const int64_t* positions, const void* q_in, int64_t q_in_stride, void* q_out,

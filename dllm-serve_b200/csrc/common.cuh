@@ -72,6 +72,19 @@ DLLM_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the phase with the given parity (no suspend).
+DLLM_DEVICE bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Time limit for any single mbarrier wait. A healthy wait in these kernels
 // lasts microseconds; the limit only ends a wait that can never complete.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
@@ -136,6 +149,39 @@ DLLM_DEVICE void tma_prefetch_desc(const void* tmap) {
 DLLM_DEVICE void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 DLLM_DEVICE void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Host: launches `kernel` with programmatic stream serialization (it may start
+// while the previous grid in the stream finishes; the kernel calls
+// griddep_wait() before reading anything that grid wrote) and, when
+// cluster_x > 1, thread-block clusters of cluster_x CTAs along x.
+template <typename Kernel, typename... Args>
+inline cudaError_t launch_pdl_cluster(Kernel kernel, dim3 grid, dim3 block, size_t smem,
+                                      cudaStream_t stream, int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <typename Kernel, typename... Args>
+inline cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  return launch_pdl_cluster(kernel, grid, block, smem, stream, 1, args...);
+}
 // 3-D tiled load, completes tx bytes on `bar`. No multicast.
 DLLM_DEVICE void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1, int c2,
                              uint64_t cache_hint) {
@@ -330,6 +376,42 @@ DLLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+
+// bf16 x 8 (one 16-byte vector) <-> fp32 x 8.
+DLLM_DEVICE void bf16x8_to_f32(uint4 w, float (&x)[8]) {
+  x[0] = __uint_as_float(w.x << 16);
+  x[1] = __uint_as_float(w.x & 0xffff0000u);
+  x[2] = __uint_as_float(w.y << 16);
+  x[3] = __uint_as_float(w.y & 0xffff0000u);
+  x[4] = __uint_as_float(w.z << 16);
+  x[5] = __uint_as_float(w.z & 0xffff0000u);
+  x[6] = __uint_as_float(w.w << 16);
+  x[7] = __uint_as_float(w.w & 0xffff0000u);
+}
+
+// NeoX rotation of 8 dimension pairs (x1 from the first half of a head row,
+// x2 from the second): y1 = x1*cos - x2*sin, y2 = x2*cos + x1*sin in fp32
+// with every product and sum rounded separately (no fused multiply-add), then
+// rounded to bf16 -- the reference's elementwise fp32 ops, bit for bit
+// (dllmserve/layers/rotary_embedding.py:6-16).
+DLLM_DEVICE void rope_rotate8(uint4& w1, uint4& w2, const float (&c)[8], const float (&s)[8]) {
+  float x1[8], x2[8];
+  bf16x8_to_f32(w1, x1);
+  bf16x8_to_f32(w2, x2);
+  uint32_t o1[4], o2[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float a0 = __fsub_rn(__fmul_rn(x1[2 * i], c[2 * i]), __fmul_rn(x2[2 * i], s[2 * i]));
+    const float a1 = __fsub_rn(__fmul_rn(x1[2 * i + 1], c[2 * i + 1]), __fmul_rn(x2[2 * i + 1], s[2 * i + 1]));
+    const float b0 = __fadd_rn(__fmul_rn(x2[2 * i], c[2 * i]), __fmul_rn(x1[2 * i], s[2 * i]));
+    const float b1 = __fadd_rn(__fmul_rn(x2[2 * i + 1], c[2 * i + 1]), __fmul_rn(x1[2 * i + 1], s[2 * i + 1]));
+    o1[i] = pack_bf16x2(a0, a1);
+    o2[i] = pack_bf16x2(b0, b1);
+  }
+  w1 = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  w2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+}
+
 
 // Packed two-lane fp32 arithmetic (Blackwell f32x2). A pair lives in one
 // 64-bit register (low half = first element) so chains of pair operations

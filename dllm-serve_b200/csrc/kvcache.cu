@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(256) kv_copy_kernel(KvCopyArgs a) {
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int lane = threadIdx.x & 31;
   const int64_t nvec = a.row_bytes / (int64_t)sizeof(V);
+  griddep_wait();  // inputs are read only after the previous grid in the stream finished
+  griddep_launch_dependents();
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < a.n_tokens;
        t += warps_total) {
     const int64_t slot = a.slots[t];
@@ -87,8 +89,7 @@ cudaError_t launch_typed(const KvCopyArgs& a, int num_sms, cudaStream_t stream) 
   const int64_t cap = (int64_t)num_sms * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  kv_copy_kernel<V, kStore><<<(unsigned)blocks, kWarps * 32, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kv_copy_kernel<V, kStore>, dim3((unsigned)blocks), dim3(kWarps * 32), 0, stream, a);
 }
 
 }  // namespace

@@ -24,30 +24,22 @@ constexpr int kHalf = 64;
 constexpr int kThreads = 256;
 constexpr int kHeadsPerPass = kThreads / 8;
 
-DLLM_DEVICE void bf16x8_to_f32(uint4 w, float (&x)[8]) {
-  x[0] = __uint_as_float(w.x << 16);
-  x[1] = __uint_as_float(w.x & 0xffff0000u);
-  x[2] = __uint_as_float(w.y << 16);
-  x[3] = __uint_as_float(w.y & 0xffff0000u);
-  x[4] = __uint_as_float(w.z << 16);
-  x[5] = __uint_as_float(w.z & 0xffff0000u);
-  x[6] = __uint_as_float(w.w << 16);
-  x[7] = __uint_as_float(w.w & 0xffff0000u);
-}
-
-DLLM_DEVICE uint4 f32x8_to_bf16(const float (&y)[8]) {
-  uint4 w;
-  w.x = pack_bf16x2(y[0], y[1]);
-  w.y = pack_bf16x2(y[2], y[3]);
-  w.z = pack_bf16x2(y[4], y[5]);
-  w.w = pack_bf16x2(y[6], y[7]);
-  return w;
+// Row of head h (q heads first, then k heads) of token t, input or output.
+DLLM_DEVICE const __nv_bfloat16* head_row(const RopeArgs& a, int64_t t, int h, bool out) {
+  const bool isq = h < a.Hq;
+  const int hh = isq ? h : h - a.Hq;
+  if (isq) return (out ? a.q_out : a.q_in) + t * (out ? a.q_out_stride : a.q_in_stride) + (int64_t)hh * kD;
+  return (out ? a.k_out : a.k_in) + t * (out ? a.k_out_stride : a.k_in_stride) + (int64_t)hh * kD;
 }
 
 __global__ void __launch_bounds__(kThreads) rope_kernel(RopeArgs a) {
   const int lane8 = threadIdx.x & 7;   // dims [8*lane8, 8*lane8 + 8) of each half
   const int hslot = threadIdx.x >> 3;  // head within a pass
   const int nh = a.Hq + a.Hkv;
+  // Programmatic dependent launch: inputs are read only after the previous
+  // grid in the stream finished; the next grid may start its prologue now.
+  griddep_wait();
+  griddep_launch_dependents();
   for (int64_t t = blockIdx.x; t < a.n_tokens; t += gridDim.x) {
     const int64_t pos = a.positions[t];
     const bool pos_ok = pos >= 0 && pos < a.max_position;
@@ -66,24 +58,13 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(RopeArgs a) {
       for (int i = 0; i < 8; ++i) c[i] = s[i] = 0.f;  // the rows become zero
     }
     for (int h = hslot; h < nh; h += kHeadsPerPass) {
-      const bool isq = h < a.Hq;
-      const int hh = isq ? h : h - a.Hq;
-      const __nv_bfloat16* src = isq ? a.q_in + t * a.q_in_stride + (int64_t)hh * kD
-                                     : a.k_in + t * a.k_in_stride + (int64_t)hh * kD;
-      __nv_bfloat16* dst = isq ? a.q_out + t * a.q_out_stride + (int64_t)hh * kD
-                               : a.k_out + t * a.k_out_stride + (int64_t)hh * kD;
-      const uint4 w1 = *reinterpret_cast<const uint4*>(src + 8 * lane8);
-      const uint4 w2 = *reinterpret_cast<const uint4*>(src + kHalf + 8 * lane8);
-      float x1[8], x2[8], y1[8], y2[8];
-      bf16x8_to_f32(w1, x1);
-      bf16x8_to_f32(w2, x2);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        y1[i] = __fsub_rn(__fmul_rn(x1[i], c[i]), __fmul_rn(x2[i], s[i]));
-        y2[i] = __fadd_rn(__fmul_rn(x2[i], c[i]), __fmul_rn(x1[i], s[i]));
-      }
-      *reinterpret_cast<uint4*>(dst + 8 * lane8) = f32x8_to_bf16(y1);
-      *reinterpret_cast<uint4*>(dst + kHalf + 8 * lane8) = f32x8_to_bf16(y2);
+      const __nv_bfloat16* src = head_row(a, t, h, false);
+      __nv_bfloat16* dst = const_cast<__nv_bfloat16*>(head_row(a, t, h, true));
+      uint4 w1 = *reinterpret_cast<const uint4*>(src + 8 * lane8);
+      uint4 w2 = *reinterpret_cast<const uint4*>(src + kHalf + 8 * lane8);
+      rope_rotate8(w1, w2, c, s);
+      *reinterpret_cast<uint4*>(dst + 8 * lane8) = w1;
+      *reinterpret_cast<uint4*>(dst + kHalf + 8 * lane8) = w2;
     }
   }
 }
@@ -94,8 +75,7 @@ cudaError_t launch_rope(const RopeArgs& a, int num_sms, cudaStream_t stream) {
   if (a.n_tokens <= 0) return cudaSuccess;
   const int64_t cap = (int64_t)num_sms * 8;  // 8 CTAs of 256 threads per SM
   const int grid = (int)(a.n_tokens < cap ? a.n_tokens : cap);
-  rope_kernel<<<grid, kThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(rope_kernel, dim3(grid), dim3(kThreads), 0, stream, a);
 }
 
 }  // namespace dllm

@@ -48,17 +48,6 @@ DLLM_DEVICE void bf16x4_to_f32(uint2 w, float (&x)[4]) {
   x[3] = __uint_as_float(w.y & 0xffff0000u);
 }
 
-DLLM_DEVICE void bf16x8_to_f32(uint4 w, float (&x)[8]) {
-  x[0] = __uint_as_float(w.x << 16);
-  x[1] = __uint_as_float(w.x & 0xffff0000u);
-  x[2] = __uint_as_float(w.y << 16);
-  x[3] = __uint_as_float(w.y & 0xffff0000u);
-  x[4] = __uint_as_float(w.z << 16);
-  x[5] = __uint_as_float(w.z & 0xffff0000u);
-  x[6] = __uint_as_float(w.w << 16);
-  x[7] = __uint_as_float(w.w & 0xffff0000u);
-}
-
 DLLM_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -77,6 +66,8 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   const int h = kHeadSelect ? blockIdx.x : 0;  // KV head (head_select)
   // shared ranking: rank in the sequence's cluster (0 = leader)
   const int crank = kHeadSelect ? 0 : (int)cg::this_cluster().block_rank();
+  griddep_wait();  // inputs are read only after the previous grid in the stream finished
+  griddep_launch_dependents();
   const int* d = a.seq_desc + seq * 8;
   const int tok_start = d[0], L = d[1], blk_start = d[2], blk_len = d[3];
   const int n_keep = d[4], slot_off = d[5], idx_off = d[6], pool_k = d[7];
@@ -441,23 +432,9 @@ cudaError_t launch_select_kv(const SelectArgs& a, bool head_select, int n_seqs, 
     if (e != cudaSuccess) return e;
     if (have != nullptr) *have = smem;
   }
-  if (head_select) {
-    select_kv_kernel<true><<<grid, kThreads, smem, stream>>>(a);
-    return cudaGetLastError();
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kClusterCtas;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, select_kv_kernel<false>, a);
+  if (head_select)
+    return launch_pdl(select_kv_kernel<true>, grid, dim3(kThreads), smem, stream, a);
+  return launch_pdl_cluster(select_kv_kernel<false>, grid, dim3(kThreads), smem, stream, kClusterCtas, a);
 }
 
 }  // namespace dllm

@@ -53,6 +53,11 @@ SIGNATURES = {
          _I64, _I, _I, _I, _F, _P, _P, _P],
         _I,
     ),
+    "dllm_attn_varlen_rope_fwd": (
+        [_P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P, _P,
+         _I, _I, _I64, _I64, _I, _I, _I, _F, _P, _P],
+        _I,
+    ),
     "dllm_rope_neox": (
         [_P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _I, _I, _P, _P],
         _I,

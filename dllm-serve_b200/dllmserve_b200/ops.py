@@ -194,11 +194,29 @@ def varlen_attention(
     slots: torch.Tensor | None = None,
     cu_seqlens_slots: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    rope: tuple[torch.Tensor, torch.Tensor] | None = None,
 ) -> torch.Tensor:
     """Non-causal varlen attention (bf16). With ``k_cached``/``v_cached``/
     ``cu_seqlens_c`` each sequence attends to [cached rows ; fresh rows]; with
     ``k_cache``/``v_cache``/``slots``/``cu_seqlens_slots`` the cached rows are
-    read straight from the paged cache (slots[cu[b]:cu[b+1]] for sequence b)."""
+    read straight from the paged cache (slots[cu[b]:cu[b+1]] for sequence b).
+
+    ``rope=(positions, cos_sin_cache)``: ``q`` and the fresh ``k`` are not yet
+    rotated; the result equals ``rope_neox(positions, q, k, cos_sin_cache)``
+    followed by this attention, bit for bit. Launches whose query segments fit
+    one 128-row tile rotate on chip (``dllm_attn_varlen_rope_fwd``: q and k are
+    left untouched); longer ones rotate into new tensors first."""
+    if rope is not None:
+        positions, cos_sin = rope
+        if k_cached is not None:
+            raise ValueError("rope is supported with the paged cache (k_cache/slots), not k_cached")
+        if int(max_seqlen_q) > 128:
+            qr, kr = rope_neox(positions, q, k, cos_sin)
+            return varlen_attention(qr, kr, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale,
+                                    k_cache=k_cache, v_cache=v_cache, slots=slots,
+                                    cu_seqlens_slots=cu_seqlens_slots, out=out)
+        return _varlen_attention_rope(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale,
+                                      positions, cos_sin, k_cache, v_cache, slots, cu_seqlens_slots, out)
     Hq, D = q.shape[1], q.shape[2]
     Hkv = k.shape[1]
     _check_rows("q", q, Hq, D)
@@ -225,18 +243,7 @@ def varlen_attention(
         stream = _stream_ptr()
         sched = sched_workspace(dev, stream)
         if k_cache is not None:
-            _require_cuda(q, k_cache, v_cache, slots, cu_seqlens_slots)
-            if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
-                raise ValueError("caches must be bfloat16")
-            row = Hkv * D
-            if (k_cache.stride(-1) != 1 or k_cache.numel() % row or v_cache.numel() != k_cache.numel()
-                    or not k_cache.is_contiguous() or not v_cache.is_contiguous()):
-                raise ValueError("caches must be contiguous [blocks, block_size, num_kv_heads, head_dim]")
-            for name, c in (("slots", slots), ("cu_seqlens_slots", cu_seqlens_slots)):
-                if c.dtype != torch.int32 or not c.is_contiguous():
-                    raise ValueError(f"{name} must be contiguous int32")
-            if cu_seqlens_slots.numel() != B + 1:
-                raise ValueError("cu_seqlens_slots must have batch+1 entries")
+            row = _check_paged(q, k_cache, v_cache, slots, cu_seqlens_slots, B, Hkv, D)
             rc = lib.dllm_attn_varlen_paged_fwd(
                 q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
                 k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row,
@@ -267,6 +274,74 @@ def varlen_attention(
                 k_cached.shape[0], Hq, Hkv, D, float(softmax_scale), sched, status, stream,
             )
     _native.check(rc, "varlen_attention")
+    if B > 0 and q.shape[0] > 0:
+        LAUNCHES[0] += 1
+    return out
+
+
+def _check_paged(q, k_cache, v_cache, slots, cu_seqlens_slots, B, Hkv, D) -> int:
+    """Validates the paged-cache arguments; returns the cache row length."""
+    _require_cuda(q, k_cache, v_cache, slots, cu_seqlens_slots)
+    if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise ValueError("caches must be bfloat16")
+    row = Hkv * D
+    if (k_cache.stride(-1) != 1 or k_cache.numel() % row or v_cache.numel() != k_cache.numel()
+            or not k_cache.is_contiguous() or not v_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous [blocks, block_size, num_kv_heads, head_dim]")
+    for name, c in (("slots", slots), ("cu_seqlens_slots", cu_seqlens_slots)):
+        if c.dtype != torch.int32 or not c.is_contiguous():
+            raise ValueError(f"{name} must be contiguous int32")
+    if cu_seqlens_slots.numel() != B + 1:
+        raise ValueError("cu_seqlens_slots must have batch+1 entries")
+    return row
+
+
+def _varlen_attention_rope(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale,
+                           positions, cos_sin, k_cache, v_cache, slots, cu_seqlens_slots, out):
+    """On-chip rotary + attention (dllm_attn_varlen_rope_fwd); max_seqlen_q <= 128."""
+    Hq, D = q.shape[1], q.shape[2]
+    Hkv = k.shape[1]
+    _check_rows("q", q, Hq, D)
+    _check_rows("k", k, Hkv, D)
+    _check_rows("v", v, Hkv, D)
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    dev = _require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, positions, cos_sin)
+    for name, c in (("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+        if c.dtype != torch.int32 or not c.is_contiguous():
+            raise ValueError(f"{name} must be contiguous int32")
+    if positions.dtype != torch.int64 or not positions.is_contiguous() or positions.numel() != q.shape[0]:
+        raise ValueError("positions must be contiguous int64 [num_tokens]")
+    if k.shape[0] != q.shape[0]:
+        raise ValueError("rope needs as many fresh key rows as query rows")
+    if cos_sin.dtype != torch.float32 or not cos_sin.is_contiguous() or cos_sin.dim() != 2 or cos_sin.shape[1] != D:
+        raise ValueError(f"cos_sin_cache must be contiguous float32 [max_position, {D}]")
+    B = cu_seqlens_q.numel() - 1
+    if cu_seqlens_k.numel() != B + 1:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k sizes differ")
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    else:
+        _check_rows("out", out, Hq, D)
+        if out.shape[0] != q.shape[0]:
+            raise ValueError("out must have as many rows as q")
+    lib = _native.lib()
+    status = _status_ptr(dev)
+    with _on_device(dev):
+        stream = _stream_ptr()
+        if k_cache is not None:
+            row = _check_paged(q, k_cache, v_cache, slots, cu_seqlens_slots, B, Hkv, D)
+            cache_args = (k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row,
+                          slots.data_ptr(), cu_seqlens_slots.data_ptr())
+        else:
+            cache_args = (None, None, 0, 0, None, None)
+        rc = lib.dllm_attn_varlen_rope_fwd(
+            positions.data_ptr(), cos_sin.data_ptr(), cos_sin.shape[0],
+            q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+            *cache_args, out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
+            B, int(max_seqlen_q), q.shape[0], k.shape[0], Hq, Hkv, D, float(softmax_scale), status, stream,
+        )
+    _native.check(rc, "varlen_attention(rope)")
     if B > 0 and q.shape[0] > 0:
         LAUNCHES[0] += 1
     return out

@@ -14,6 +14,10 @@
  *   dllm_attn_varlen_paged_fwd
  *                             <- the same with the cached rows read from the paged cache by
  *                                slot (load_kvcache fused in, attention.py:241-263)
+ *   dllm_attn_varlen_rope_fwd <- RotaryEmbedding.forward (rotary_embedding.py:41-57) on q and
+ *                                the fresh k, fused into the attention of a launch whose
+ *                                query segments fit one 128-row tile (the reuse steps'
+ *                                blocks): llada.py:81-84 / dream.py:90-93 in one call
  *   dllm_rope_neox            <- RotaryEmbedding.forward / apply_rotary_emb
  *                                (dllmserve/layers/rotary_embedding.py:6-16, 41-57), the
  *                                op the decoder layers apply to q, k just before attention
@@ -179,6 +183,34 @@ DLLM_API int dllm_attn_varlen_paged_fwd(const void* q, int64_t q_tok_stride, con
                                int max_seqlen_q, int64_t total_q, int64_t total_k, int num_heads,
                                int num_kv_heads, int head_dim, float softmax_scale,
                                int32_t* sched_workspace, int32_t* err_flag, void* stream);
+
+/*
+ * Rotary embedding fused into attention: the result equals dllm_rope_neox(positions, q, k)
+ * followed by dllm_attn_varlen_paged_fwd (or dllm_attn_varlen_fwd when slots is NULL) on the
+ * rotated q and k, bit for bit, but q and k are never rewritten: each query tile and each
+ * fresh key tile is rotated in shared memory between its load and the matrix multiply that
+ * reads it. Replaces the decoder layers' `q, k = self.rotary_emb(positions, q, k)` followed
+ * by `self.attn(q, k, v)` (llada.py:81-84, dream.py:90-93) for the diffusion reuse steps.
+ * positions: int64 [total_q], the position of query row r and of fresh key row r (so
+ * total_k must equal total_q). cos_sin_cache: fp32 [max_position, 128], cos | sin halves,
+ * 16-byte aligned. Cached rows (k_cache/v_cache through slots/cu_seqlens_slots, both NULL
+ * for none) are taken as already rotated, as store_kvcache wrote them. max_seqlen_q must be
+ * <= 128 (DLLM_ERR_UNSUPPORTED otherwise: rotate with dllm_rope_neox, then attend).
+ * Positions outside [0, max_position) give zero rows and flag
+ * DLLM_DEV_POSITION_OUT_OF_RANGE. No scheduler workspace (units are handed out round-robin).
+ */
+DLLM_API int dllm_attn_varlen_rope_fwd(const int64_t* positions, const float* cos_sin_cache,
+                                       int64_t max_position, const void* q, int64_t q_tok_stride,
+                                       const void* k, int64_t k_tok_stride, const void* v,
+                                       int64_t v_tok_stride, const void* k_cache,
+                                       const void* v_cache, int64_t cache_tok_stride,
+                                       int64_t num_slots, const int32_t* slots,
+                                       const int32_t* cu_seqlens_slots, void* o,
+                                       int64_t o_tok_stride, const int32_t* cu_seqlens_q,
+                                       const int32_t* cu_seqlens_k, int batch, int max_seqlen_q,
+                                       int64_t total_q, int64_t total_k, int num_heads,
+                                       int num_kv_heads, int head_dim, float softmax_scale,
+                                       int32_t* err_flag, void* stream);
 
 /*
  * NeoX rotary embedding of q and k (RotaryEmbedding.forward, rotary_embedding.py:41-57,
