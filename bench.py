@@ -418,6 +418,72 @@ def run_ours(args, lens):
         rope_block = {"kernel": "dllm::rope_kernel", "ms": ms, "GB/s": gbs, "frac_of_hbm": gbs / hbm,
                       "bytes_per_launch": byts, "tokens": N}
 
+    # ---------------- RoPE fused into a reuse-step attention launch ----------------
+    rope_fused = None
+    if not args.skip_extras:
+        # config-3 reuse step: 8 sequences, 32-token block, 304 cached rows each
+        B3, blk, nkeep, L3 = 8, 32, 304, 16
+        n3 = B3 * blk
+        pages3 = (B3 * nkeep + 255) // 256 + 1
+        kc3 = torch.randn(pages3, 256, Hk, HEAD_DIM, device=dev, dtype=torch.bfloat16, generator=gen)
+        vc3 = torch.randn(pages3, 256, Hk, HEAD_DIM, device=dev, dtype=torch.bfloat16, generator=gen)
+        paged3 = dict(k_cache=kc3, v_cache=vc3,
+                      slots=torch.arange(B3 * nkeep, dtype=torch.int32, device=dev),
+                      cu_seqlens_slots=torch.arange(0, B3 * nkeep + 1, nkeep, dtype=torch.int32, device=dev))
+        cq3 = torch.arange(0, n3 + 1, blk, dtype=torch.int32, device=dev)
+        q3 = [torch.randn(n3, Hq, HEAD_DIM, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(L3)]
+        k3 = [torch.randn(n3, Hk, HEAD_DIM, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(L3)]
+        v3 = [torch.randn(n3, Hk, HEAD_DIM, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(L3)]
+        pos3 = torch.cat([torch.arange(nkeep, nkeep + blk) for _ in range(B3)]).to(dev)
+        out3 = torch.empty(n3, Hq, HEAD_DIM, device=dev, dtype=torch.bfloat16)
+        qo3, ko3 = torch.empty_like(q3[0]), torch.empty_like(k3[0])
+        cs = rope.cos_sin_cache
+
+        def r_unfused():
+            for l in range(L3):
+                ops.rope_neox(pos3, q3[l], k3[l], cs, query_out=qo3, key_out=ko3)
+                ops.varlen_attention(qo3, ko3, v3[l], cq3, cq3, blk, scale, out=out3, **paged3)
+
+        def r_fused():
+            for l in range(L3):
+                ops.varlen_attention(q3[l], k3[l], v3[l], cq3, cq3, blk, scale, out=out3,
+                                     rope=(pos3, cs), **paged3)
+
+        def r_attn():
+            for l in range(L3):
+                ops.varlen_attention(q3[l], k3[l], v3[l], cq3, cq3, blk, scale, out=out3, **paged3)
+
+        r_unfused()
+        ref3 = out3.clone()
+        r_fused()
+        same = bool(torch.equal(out3, ref3))
+        us = {}
+        for tag, fn in (("rope_then_attention", r_unfused), ("fused", r_fused), ("attention_only", r_attn)):
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            for _ in range(3):
+                graph.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record(stream)
+            for _ in range(20):
+                graph.replay()
+            b.record(stream)
+            torch.cuda.synchronize()
+            us[tag] = a.elapsed_time(b) * 1000 / (20 * L3)
+            del graph
+        rope_fused = {"workload": f"config-3 reuse-step layer: {B3} x {blk}-token blocks, {nkeep} cached rows, "
+                                  f"{Hq}/{Hk} heads, CUDA graph of {L3} layers",
+                      "us_per_layer": us, "fused_equals_unfused": same,
+                      "fused_entry": "dllm_attn_varlen_rope_fwd (opt-in; the layer uses rope_then_attention)"}
+
     # ---------------- TP layer: attention + o_proj + all-reduce ----------------
     tp_block = None
     if not args.skip_extras:
@@ -535,7 +601,8 @@ def run_ours(args, lens):
             "config": config_block(lens, world),
             "step_tokens_per_s": tokens_per_s,
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": launches, "kv_store": kv_block, "rope": rope_block, "tp_layer": tp_block,
+            "gpu_launches": launches, "kv_store": kv_block, "rope": rope_block,
+            "rope_fused_reuse": rope_fused, "tp_layer": tp_block,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
