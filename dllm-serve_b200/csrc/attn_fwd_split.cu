@@ -646,85 +646,42 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
     __syncwarp();
   } else if (warp == 11) {
     // ------------------------------------------------------------- rotary
-    // (rotary launches only) Two independent in-order streams, polled: the Q
-    // loads (each rotated and released on its stage's QROPED barrier) and the
-    // fresh K loads (each completes on its stage's KFRESH barrier and is
-    // rotated and released on KROPED). A stage holding a Q tile or a fresh K
-    // tile is refilled only after the MMA warp consumed it, which needs this
-    // warp's release, so neither barrier can run two phases ahead of this
-    // warp. Cached K tiles were rotated before they were stored; they bypass
-    // this warp (only counted, for the ring positions). Polling both streams
-    // lets the next unit's Q be rotated as soon as it lands.
-    int uq = blockIdx.x, uk = blockIdx.x, jk = 0;
+    // (rotary launches only) Follows the producer's order: the unit's Q tile
+    // (rotated and released on its stage's QROPED barrier), then its fresh K
+    // tiles (each completes on its stage's KFRESH barrier and is rotated and
+    // released on KROPED); cached K tiles were rotated before they were
+    // stored and bypass this warp (only counted, for the ring positions). A
+    // stage holding a Q tile or a fresh K tile is refilled only after the MMA
+    // warp consumed it, which needs this warp's release, so neither barrier
+    // can run two phases ahead of this warp. The producer issues the next
+    // unit's Q right after this unit's last K tile, about two KV tiles before
+    // the unit ends, so the next Q is rotated off the critical path.
     uint32_t q_it = 0, k_it = 0, kf_par = 0;
-    Unit tq{}, tk{};
-    KvTile kcur{};
-    auto next_q = [&]() {
-      for (; uq < total_units; uq += gridDim.x) {
-        tq = decode_unit(uq, args);
-        if (tq.valid) return true;
-      }
-      return false;
-    };
-    // Moves the K cursor (uk, jk, k_it) to the next fresh tile at or after it.
-    bool k_in_unit = false;
-    auto next_fresh_k = [&]() {
-      while (true) {
-        if (!k_in_unit) {
-          for (; uk < total_units; uk += gridDim.x) {
-            tk = decode_unit(uk, args);
-            if (tk.valid && tk.nkv > 0) break;
-          }
-          if (uk >= total_units) return false;
-          k_in_unit = true;
-          jk = 0;
-        }
-        for (; jk < tk.nkv; ++jk, ++k_it) {
-          kcur = kv_tile(jk, tk.nc, tk.c_begin, tk.nk, tk.k_begin);
-          if (kcur.seg == 1) return true;
-        }
-        k_in_unit = false;
-        uk += gridDim.x;
-      }
-    };
-    bool q_more = next_q(), k_more = next_fresh_k();
-    uint64_t t_last = globaltimer_ns();
-    while ((q_more || k_more) && !*abort_flag) {
-      bool progressed = false;
-      if (k_more) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      const Unit t = decode_unit(u, args);
+      if (!t.valid) continue;
+      const int qs = q_it % kStagesQ;
+      ok = mbar_wait_warp(bar(BAR_QFULL + qs), (q_it / kStagesQ) & 1, abort_flag);
+      if (!ok) break;
+      ++q_it;
+      rope_tile_smem(smem + kOffQ + qs * kTileBytes, lane, args, (int64_t)t.q_begin + t.q0,
+                     min(t.Lq - t.q0, kTileM / args.qpack), args.qpack, t.nheads);
+      fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_QROPED + qs));
+      for (int j = 0; j < t.nkv && ok; ++j, ++k_it) {
+        const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
+        if (kt.seg != 1) continue;
         const int kst = k_it % kStagesK;
         const uint32_t bit = 1u << kst;
-        if (__all_sync(0xffffffffu, mbar_test_wait(bar(BAR_KFRESH + kst), (kf_par & bit) ? 1u : 0u))) {
-          rope_tile_smem(smem + kOffK + kst * kTileBytes, lane, args, kcur.row0, kcur.valid, 1, 1);
-          fence_proxy_async_smem();  // generic-proxy writes -> tensor-core reads
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(BAR_KROPED + kst));
-          kf_par ^= bit;
-          ++jk;
-          ++k_it;
-          k_more = next_fresh_k();
-          progressed = true;
-        }
-      }
-      if (q_more) {
-        const int qs = q_it % kStagesQ;
-        if (__all_sync(0xffffffffu, mbar_test_wait(bar(BAR_QFULL + qs), (q_it / kStagesQ) & 1))) {
-          rope_tile_smem(smem + kOffQ + qs * kTileBytes, lane, args, (int64_t)tq.q_begin + tq.q0,
-                         min(tq.Lq - tq.q0, kTileM / args.qpack), args.qpack, tq.nheads);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(BAR_QROPED + qs));
-          ++q_it;
-          uq += gridDim.x;
-          q_more = next_q();
-          progressed = true;
-        }
-      }
-      if (progressed) {
-        t_last = globaltimer_ns();
-      } else {
-        __nanosleep(64);
-        if (globaltimer_ns() - t_last > kWaitLimitNs) *abort_flag = 1;
+        ok = mbar_wait_warp(bar(BAR_KFRESH + kst), (kf_par & bit) ? 1u : 0u, abort_flag);
+        if (!ok) break;
+        kf_par ^= bit;
+        rope_tile_smem(smem + kOffK + kst * kTileBytes, lane, args, kt.row0, kt.valid, 1, 1);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(BAR_KROPED + kst));
       }
     }
     __syncwarp();
