@@ -357,6 +357,85 @@ def test_attention_c2_full_size_sampled(dev):
     _status_clear(dev)
 
 
+def _sampled_check(out, q, k, v, cu, pairs, group=1, kc=None, vc=None, cuc=None):
+    """(sequence, query head) pairs of a full-size launch against the oracle;
+    with kc/vc/cuc the keys of sequence b are [cached rows ; fresh rows]."""
+    D = q.shape[2]
+    for b, h in pairs:
+        s0, s1 = cu[b], cu[b + 1]
+        hk = h // group
+        kk, vv = k[s0:s1, hk:hk + 1].cpu(), v[s0:s1, hk:hk + 1].cpu()
+        if kc is not None:
+            c0, c1 = cuc[b], cuc[b + 1]
+            kk = torch.cat([kc[c0:c1, hk:hk + 1].cpu(), kk])
+            vv = torch.cat([vc[c0:c1, hk:hk + 1].cpu(), vv])
+        ref = R.sdpa_seq(q[s0:s1, h:h + 1].cpu(), kk, vv, D ** -0.5)
+        _check_attn(out[s0:s1, h:h + 1], ref, f"seq {b} head {h}")
+
+
+def test_attention_c5_dense_full_size_sampled(dev):
+    """Config-5 dense step shape (B=8, L=4,608, 32 MHA heads; 2.78 TFLOP per
+    layer): every output row finite, sampled pairs against the oracle."""
+    D, H, lens = 128, 32, [4608] * 8
+    N = sum(lens)
+    gd = torch.Generator(device=dev).manual_seed(51)
+    q, k, v = (torch.randn(N, H, D, device=dev, dtype=torch.bfloat16, generator=gd) for _ in range(3))
+    cu = _cu(lens)
+    cud = torch.tensor(cu, dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(q, k, v, cud, cud, max(lens))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    _sampled_check(out, q, k, v, cu, [(0, 0), (5, 17), (7, 31)])
+    _status_clear(dev)
+
+
+def test_attention_c5_reuse_full_size_sampled(dev):
+    """Config-5 reuse step (8 sequences: 1,144 selected rows read from the paged
+    cache by slot + the 32-row block, 32 heads), slots scattered over pages."""
+    D, H, blk, n_keep, B = 128, 32, 32, 1144, 8
+    gd = torch.Generator(device=dev).manual_seed(52)
+    pages = (B * n_keep + 255) // 256 + 3
+    kc = torch.randn(pages, 256, H, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    vc = torch.randn(pages, 256, H, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    perm = torch.randperm(pages * 256, device=dev, generator=gd)[:B * n_keep].to(torch.int32)
+    # half the sequences on consecutive slots (TMA path), half scattered (gather path)
+    slots = torch.cat([torch.arange(b * n_keep, (b + 1) * n_keep, device=dev, dtype=torch.int32)
+                       if b % 2 == 0 else perm[b * n_keep:(b + 1) * n_keep] for b in range(B)])
+    N = B * blk
+    q, k, v = (torch.randn(N, H, D, device=dev, dtype=torch.bfloat16, generator=gd) for _ in range(3))
+    cu, cuc = _cu([blk] * B), _cu([n_keep] * B)
+    out = _ops().varlen_attention(q, k, v, torch.tensor(cu, dtype=torch.int32, device=dev),
+                                  torch.tensor(cu, dtype=torch.int32, device=dev), blk,
+                                  k_cache=kc, v_cache=vc, slots=slots,
+                                  cu_seqlens_slots=torch.tensor(cuc, dtype=torch.int32, device=dev))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    rows_k = kc.view(-1, H, D)[slots.long()]
+    rows_v = vc.view(-1, H, D)[slots.long()]
+    _sampled_check(out, q, k, v, cu, [(0, 3), (1, 30), (6, 11), (7, 0)], kc=rows_k, vc=rows_v, cuc=cuc)
+    _status_clear(dev)
+
+
+def test_attention_c4_dense_full_size_sampled(dev):
+    """Config-4 dense step shape (Dream-7B GQA 28/4, B=32, prompt U[128,768] +
+    256 generated tokens): sampled (sequence, query head) pairs."""
+    D, Hq, Hkv = 128, 28, 4
+    g = torch.Generator().manual_seed(4)
+    lens = [int(p) + 256 for p in torch.randint(128, 769, (32,), generator=g)]
+    N = sum(lens)
+    gd = torch.Generator(device=dev).manual_seed(53)
+    q = torch.randn(N, Hq, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    k = torch.randn(N, Hkv, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    v = torch.randn(N, Hkv, D, device=dev, dtype=torch.bfloat16, generator=gd)
+    cu = _cu(lens)
+    cud = torch.tensor(cu, dtype=torch.int32, device=dev)
+    out = _ops().varlen_attention(q, k, v, cud, cud, max(lens))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    _sampled_check(out, q, k, v, cu, [(0, 0), (9, 6), (20, 13), (31, 27)], group=Hq // Hkv)
+    _status_clear(dev)
+
+
 def test_attention_rejects_bad_args(dev):
     ops = _ops()
     q = torch.zeros(4, 2, 64, dtype=torch.bfloat16, device=dev)
