@@ -26,9 +26,32 @@ def head_slice(num_heads: int, num_kv_heads: int, rank: int, world: int) -> tupl
 
 
 def row_parallel_oproj(x: torch.Tensor, weight_shard: torch.Tensor, bias: torch.Tensor | None = None,
-                       rank: int = 0, group=None) -> torch.Tensor:
-    """y = x @ W_shard^T (+ bias on rank 0), summed over ranks (linear.py:186-190)."""
-    y = F.linear(x, weight_shard, bias if rank == 0 else None)
-    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
-        dist.all_reduce(y, group=group)
+                       rank: int = 0, group=None, chunks: int = 1) -> torch.Tensor:
+    """y = x @ W_shard^T (+ bias on rank 0), summed over ranks (linear.py:186-190).
+
+    ``chunks`` > 1 splits the rows: each chunk's GEMM is followed by an
+    asynchronous all-reduce of that chunk, which runs on NCCL's stream while
+    the next chunk's GEMM runs on the current one. The all-reduce is
+    elementwise, so chunking changes nothing it sums; a chunk's GEMM may
+    round differently from the whole one (the library picks its algorithm
+    per shape)."""
+    distributed = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
+    b = bias if rank == 0 else None
+    if not distributed or chunks <= 1 or x.shape[0] < chunks:
+        y = F.linear(x, weight_shard, b)
+        if distributed:
+            dist.all_reduce(y, group=group)
+        return y
+    y = torch.empty(x.shape[0], weight_shard.shape[0], dtype=x.dtype, device=x.device)
+    bounds = [x.shape[0] * i // chunks for i in range(chunks + 1)]
+    works = []
+    for i in range(chunks):
+        r0, r1 = bounds[i], bounds[i + 1]
+        if b is not None:
+            torch.addmm(b, x[r0:r1], weight_shard.t(), out=y[r0:r1])
+        else:
+            torch.matmul(x[r0:r1], weight_shard.t(), out=y[r0:r1])
+        works.append(dist.all_reduce(y[r0:r1], group=group, async_op=True))
+    for w in works:
+        w.wait()
     return y

@@ -100,7 +100,9 @@ def _tp_worker(rank, world, port, q, k, v, w, lens, out_path):
             cu.append(cu[-1] + L)
         o = R.varlen_attention(q[:, h0:h1], k[:, k0:k1], v[:, k0:k1], cu, cu, D ** -0.5)
         y = row_parallel_oproj(o.reshape(o.shape[0], -1), w[:, h0 * D:h1 * D], rank=rank)
-        torch.save({"rank": rank, "attn": o, "y": y}, f"{out_path}.{rank}")
+        # rows split in 3 chunks, each all-reduced asynchronously after its GEMM
+        y3 = row_parallel_oproj(o.reshape(o.shape[0], -1), w[:, h0 * D:h1 * D], rank=rank, chunks=3)
+        torch.save({"rank": rank, "attn": o, "y": y, "y3": y3}, f"{out_path}.{rank}")
     finally:
         dist.destroy_process_group()
 
@@ -130,3 +132,4 @@ def test_head_sharded_tp_matches_single_process(tmp_path, hq, hkv):
         torch.testing.assert_close(res["attn"], full[:, r * per_rank:(r + 1) * per_rank])
         # the all-reduced row-parallel o_proj equals the single-process o_proj
         torch.testing.assert_close(res["y"], y_ref, rtol=1e-4, atol=1e-4)
+        torch.testing.assert_close(res["y3"], y_ref, rtol=1e-4, atol=1e-4)
