@@ -29,8 +29,10 @@
  * Conventions
  *   - Every pointer except `err_flag`/`top_idx` arguments documented as optional is a
  *     device pointer owned by the caller. The library never allocates or frees memory,
- *     never synchronises the stream and never reads device data on the host, so every
- *     call can be captured in a CUDA graph.
+ *     never synchronises the stream and never reads device data on the host, so a call
+ *     of any entry point that works only on caller buffers can be captured in a CUDA
+ *     graph (dllm_attn_varlen_fwd_static_ws, which uses a library array, is not one of
+ *     them).
  *   - `stream` is a cudaStream_t passed as void*. NULL means the legacy default stream.
  *   - Strides are in ELEMENTS unless the name ends in `_bytes`.
  *   - bf16 tensors are laid out [tokens, heads, head_dim] with head_dim contiguous and
