@@ -98,3 +98,27 @@ def test_ops_refuse_cpu_tensors():
     cu = torch.tensor([0, 4], dtype=torch.int32)
     with pytest.raises(ValueError, match="CUDA"):
         ops.varlen_attention(q, q, q, cu, cu, 4)
+
+
+def test_rope_attention_validation_without_gpu():
+    """dllm_attn_varlen_rope_fwd refuses bad arguments before any device work."""
+    lib = _native.lib()
+    f = ctypes.c_float(0.1)
+
+    def call(positions=1, cos_sin=16, max_pos=16, slots=None, cu_slots=None, num_slots=0,
+             batch=1, max_q=32, total_q=32, total_k=32, hd=128):
+        return lib.dllm_attn_varlen_rope_fwd(
+            positions, cos_sin, max_pos, None, 0, None, 0, None, 0, None, None, 0, num_slots,
+            slots, cu_slots, None, 0, None, None, batch, max_q, total_q, total_k, 4, 4, hd, f, None, None)
+
+    assert call(positions=None) == _native.DLLM_ERR_INVALID_ARG
+    assert "positions" in lib.dllm_last_error().decode()
+    assert call(slots=64, cu_slots=None) == _native.DLLM_ERR_INVALID_ARG  # slots without their offsets
+    assert call(slots=64, cu_slots=64, num_slots=0) == _native.DLLM_ERR_INVALID_ARG
+    assert call(cos_sin=None) == _native.DLLM_ERR_INVALID_ARG
+    assert call(cos_sin=8) == _native.DLLM_ERR_ALIGNMENT  # cos/sin rows are read 16 bytes at a time
+    assert call(max_q=129, total_q=129, total_k=129) == _native.DLLM_ERR_UNSUPPORTED
+    assert "rotate first" in lib.dllm_last_error().decode()
+    assert call(total_k=31) == _native.DLLM_ERR_INVALID_ARG  # one position per query and key row
+    assert call(hd=64) == _native.DLLM_ERR_UNSUPPORTED
+    assert call(batch=0, max_q=0, total_q=0, total_k=0) == _native.DLLM_OK  # empty: no-op
