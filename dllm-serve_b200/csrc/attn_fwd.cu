@@ -32,9 +32,6 @@ namespace {
 constexpr int kD = 128;          // head dim (only 128 is instantiated)
 constexpr int kTileM = 128;      // query rows per tile
 constexpr int kTileN = 128;      // kv rows per tile
-#ifndef DLLM_EPI_QUAD
-#define DLLM_EPI_QUAD 1  // lane-quad transposed output stores
-#endif
 constexpr int kStagesK = 3;      // K ring depth (K runs one tile ahead of V)
 constexpr int kStagesV = 2;      // V ring depth
 constexpr int kThreads = 352;
@@ -649,7 +646,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_in_tile == 0) TRACE(14, 0, wg);
         tc_fence_after();
         const float inv_l = 1.f / l;
-#if DLLM_EPI_QUAD
         // Rows are spread one per lane; a 4x4 transpose of 16-byte vectors
         // inside each lane quad lets every store instruction write 8 rows x 64
         // contiguous bytes (full sectors) instead of 32 rows x 16 bytes.
@@ -677,26 +673,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-#else
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld();
-          if (row_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
-              w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
-              w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
-              w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
-              dst[v] = w;
-            }
-          }
-        }
-#endif
         // O_i is read out; the next unit's first PV may overwrite it once this
         // warpgroup arrives on its first P barrier (program order + fence).
         tc_fence_before();
