@@ -772,7 +772,12 @@ def run_sparse_cycle(args):
             s.sparse_state.cache_state = st
             s.sparse_state.step_in_block = st
         ctxs[st] = make_ctx(sparse_seqs)
-        step(sparse_seqs, ctxs[st])  # builds and caches the plan outside capture
+        # One eager step on the capture stream: builds and caches the plan
+        # outside capture and gives the stream its scheduler workspace, so the
+        # captured attention launches hand out units dynamically.
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step(sparse_seqs, ctxs[st])
         torch.cuda.synchronize()
         g_ = torch.cuda.CUDAGraph()
         side.wait_stream(torch.cuda.current_stream())
@@ -787,7 +792,9 @@ def run_sparse_cycle(args):
         [timed(lambda: [graphs[st].replay() for st in order], 1) for _ in range(max(2, cycles))])
     graph_dense = torch.cuda.CUDAGraph()
     ctx_d = make_ctx(dense_seqs)
-    step(dense_seqs, ctx_d)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(dense_seqs, ctx_d)  # plan + the capture stream's scheduler workspace
     torch.cuda.synchronize()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
