@@ -651,11 +651,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // contiguous bytes (full sectors) instead of 32 rows x 16 bytes.
         const int qj = lane & 3;
         const int qrow0 = row - qj;  // first row of this lane's quad
+        // TMEM loads run one chunk ahead of the conversion and stores.
+        uint32_t onext[32];
+        tmem_ld32(tO, onext);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = onext[e];
+          if (c < 3) tmem_ld32(tO + (c + 1) * 32, onext);
           uint4 v[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
