@@ -34,14 +34,18 @@ def test_c1_rope_dense_attention_matches_reference(golden_dir):
     L = c["prompt_len"] + c["gen_len"]
     H, D = c["num_heads"], c["head_dim"]
     q, k, v = (torch.randn((L, H, D), generator=g) for _ in range(3))
-    assert np.allclose(I.checksum(q) + I.checksum(k) + I.checksum(v), gold["input_checksums"])
+    got = np.array(I.checksum(q) + I.checksum(k) + I.checksum(v))
+    assert np.allclose(got, gold["input_checksums"]), f"input checksums {got} vs {gold['input_checksums']}"
     cache = R.rope_cache(D, L, c["rope_theta"])
     pos = torch.arange(L)
     qr, kr = R.apply_rope(q, pos, cache), R.apply_rope(k, pos, cache)
-    assert np.allclose(I.checksum(qr) + I.checksum(kr), gold["rope_checksums"], rtol=1e-6)
+    got = np.array(I.checksum(qr) + I.checksum(kr))
+    assert np.allclose(got, gold["rope_checksums"], rtol=1e-6), (
+        f"rope checksums {got} vs {gold['rope_checksums']}")
     out = R.varlen_attention(qr, kr, v, [0, L], [0, L], D ** -0.5)
     err = np.abs(out.numpy() - gold["out"].astype(np.float32))
-    assert err.max() < ATOL
+    assert err.max() < ATOL, (f"max abs error {err.max():.3e} at {np.unravel_index(err.argmax(), err.shape)}, "
+                              f"torch threads {torch.get_num_threads()}")
 
 
 def _build_step(case, g, step):
