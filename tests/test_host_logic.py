@@ -116,3 +116,83 @@ def test_head_slice():
     assert head_slice(28, 4, 3, 4) == (21, 28, 3, 4)
     with pytest.raises(ValueError):
         head_slice(28, 4, 0, 8)  # Dream's 4 KV heads do not split 8 ways
+
+
+def test_step_plan_matches_oracle_rules_on_random_batches():
+    """Property test: for random batches of dense, compute-cache and reuse
+    sequences, the step plan's rows, offsets, cached-row counts, slot order and
+    selection descriptors equal those the oracle's restatement of the
+    reference's per-sequence rules (SeqMeta, attention.py:168-304) gives."""
+    hypothesis = pytest.importorskip("hypothesis")
+    from hypothesis import given, settings, strategies as st
+    from oracle import attention_ref as R
+
+    seq_st = st.tuples(
+        st.integers(1, 300),                      # prompt length
+        st.sampled_from([16, 32]),                # block length
+        st.integers(1, 4),                        # generated blocks
+        st.sampled_from([None, 1, 2]),            # None: no sparse state (dense); else cache state
+        st.integers(0, 3),                        # current block index (clamped below)
+        st.sampled_from([0.0, 0.25, 0.5, 1.0]),   # retention ratio
+        st.sampled_from([1, 3, 4, 5]),            # pool kernel
+        st.booleans(),                            # head_select
+    )
+
+    @settings(max_examples=200, deadline=None)
+    @given(st.lists(seq_st, min_size=1, max_size=8), st.sampled_from([1, 2, 4, 8]))
+    def check(specs, hkv):
+        seqs, metas, slots = [], [], []
+        base = 0
+        for prompt, blen, nblk, state, bidx, ratio, pool, hs in specs:
+            gen = blen * nblk
+            bidx = min(bidx, nblk - 1)
+            if state is None:
+                s = _Seq(prompt, gen, None)
+                m = R.SeqMeta(state=0, num_tokens=prompt + gen, prompt_len=prompt)
+            else:
+                cfg = SparseConfig(enabled=True, default_block_len=blen, retention_ratio=ratio,
+                                   pool_kernel=pool, head_select=hs)
+                s = _Seq(prompt, gen, cfg, state=state, block_idx=bidx)
+                m = R.SeqMeta(state=state, num_tokens=prompt + gen, prompt_len=prompt, block_idx=bidx,
+                              block_len=blen, ratio=ratio, pool_kernel=pool, head_select=hs)
+            n = m.n_keep() if m.state else 0
+            slots.append(torch.arange(base, base + n, dtype=torch.int32) if m.state else [])
+            base += n
+            seqs.append(s)
+            metas.append(m)
+        rows = sum(m.rows() for m in metas)
+        plan = build_step_plan(types.SimpleNamespace(seqs=seqs, slot_mapping=slots), torch.device("cpu"), rows)
+        cu = [0]
+        for m in metas:
+            cu.append(cu[-1] + m.rows())
+        assert plan.cu.tolist() == cu
+        assert plan.max_rows == max(m.rows() for m in metas)
+        reuse = [i for i, m in enumerate(metas) if m.state == 2]
+        if reuse:
+            cc = [0]
+            for m in metas:
+                cc.append(cc[-1] + (m.n_keep() if m.state == 2 else 0))
+            assert plan.cu_c.tolist() == cc
+            assert plan.slots_c.tolist() == [x for i in reuse for x in slots[i].tolist()]
+        else:
+            assert plan.cu_c is None and plan.total_c == 0
+        for hs in (True, False):
+            idx = [i for i, m in enumerate(metas) if m.state == 1 and m.head_select == hs]
+            arrs = selection_arrays(plan, hs, hkv, torch.device("cpu"))
+            if not idx:
+                assert arrs is None
+                continue
+            desc, sl, max_klen, total = arrs
+            want, slot_off, idx_off = [], 0, 0
+            for i in idx:
+                m = metas[i]
+                bs, bl = m.block()
+                want.append([cu[i], m.num_tokens, bs, bl, m.n_keep(), slot_off, idx_off, m.pool_kernel])
+                slot_off += m.n_keep()
+                idx_off += m.n_keep() * (hkv if hs else 1)
+            assert desc.tolist() == want
+            assert total == idx_off
+            assert max_klen == max(metas[i].num_tokens - metas[i].block()[1] for i in idx)
+            assert sl.tolist() == [x for i in idx for x in slots[i].tolist()]
+
+    check()
