@@ -8,6 +8,10 @@
  *   dllm_store_kvcache        <- store_kvcache + store_kvcache_kernel   (attention.py:11-50)
  *   dllm_load_kvcache         <- load_kvcache + load_kvcache_kernel     (attention.py:53-92)
  *   dllm_attn_varlen_fwd      <- flash_attn_varlen_func(..., causal=False) (attention.py:289-299)
+ *   dllm_attn_varlen_fwd_static_ws
+ *                             (no reference counterpart) dllm_attn_varlen_fwd for callers
+ *                                that cannot allocate device memory: its scheduler workspace
+ *                                is a small array inside the library (see its declaration)
  *   dllm_attn_varlen_cached_fwd
  *                             <- reuse-state K/V assembly + varlen call (attention.py:235-299):
  *                                keys are [cached selected rows ; fresh block rows]
