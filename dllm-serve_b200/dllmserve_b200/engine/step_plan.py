@@ -80,18 +80,6 @@ class StepPlan:
     def k_lens(self):
         return [i.rows + i.n_cached for i in self.infos]
 
-    def cached_buffers(self, num_kv_heads: int, head_dim: int, dtype, device):
-        """Scratch rows for the gathered cached K/V of state-2 sequences,
-        shared by all layers of the step (stream-ordered reuse)."""
-        key = (num_kv_heads, head_dim, dtype)
-        buf = self.scratch.get(key)
-        if buf is None:
-            shape = (self.total_c, num_kv_heads, head_dim)
-            buf = (torch.empty(shape, dtype=dtype, device=device),
-                   torch.empty(shape, dtype=dtype, device=device))
-            self.scratch[key] = buf
-        return buf
-
 
 def _h2d(values, device, dtype=torch.int32) -> torch.Tensor:
     t = torch.tensor(values, dtype=dtype)

@@ -6,8 +6,6 @@ The tensors must live on a CUDA device; there is no CPU path.
 """
 from __future__ import annotations
 
-import math
-
 import torch
 
 from . import _native
@@ -442,11 +440,3 @@ def select_kv_store(
     if seq_desc.shape[0] > 0 and max_klen > 0:
         LAUNCHES[0] += 1
 
-
-def attention_flops(q_lens, k_lens, num_heads: int, head_dim: int) -> float:
-    """4 * sum(Lq * Lk) * Hq * D (non-causal; QK^T and PV)."""
-    return 4.0 * float(sum(int(a) * int(b) for a, b in zip(q_lens, k_lens))) * num_heads * head_dim
-
-
-def default_scale(head_dim: int) -> float:
-    return 1.0 / math.sqrt(head_dim)
