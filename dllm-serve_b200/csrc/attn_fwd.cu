@@ -22,6 +22,8 @@
 //   segment 0: cached rows (k_cache/v_cache gathered rows, `cu_c`), optional
 //   segment 1: fresh rows of the step's k/v (`cu_k`)
 // KV tiles never straddle segments; a partial tile uses a smaller MMA N.
+#include <atomic>
+
 #include "common.cuh"
 #include "attn_fwd.h"
 
@@ -36,11 +38,6 @@ constexpr int kStagesK = 3;      // K ring depth (K runs one tile ahead of V)
 constexpr int kStagesV = 2;      // V ring depth
 constexpr int kThreads = 352;
 
-// Softmax code-shape switches (tuning; defaults are the measured best).
-#ifndef DLLM_SM_POLY
-#define DLLM_SM_POLY 0
-#endif
-constexpr int kSmPoly = DLLM_SM_POLY;         // pairs of 8 evaluated on the FMA pipe
 constexpr uint32_t kTileBytes = kTileM * kD * 2;  // 32 KB (bf16)
 constexpr uint32_t kChunkBytes = 128 * 128;       // 128 rows x 128 B (64 bf16)
 
@@ -95,75 +92,26 @@ DLLM_DEVICE KvTile kv_tile(int t, int nc, int c0, int nk, int k0) {
   return r;
 }
 
-#ifdef DLLM_TRACE
-// Debug-only event trace (never built into the shipped library): for every
-// 256th CTA (up to 16) each warp records (clock64, code) pairs into its own
-// slice after the status word; per-warp counters live in shared memory.
-__shared__ unsigned g_trace_cnt[16];
-DLLM_DEVICE void trace_rec(int32_t* err, int ev, int j, int tile) {
-  const unsigned cid = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-  if (err == nullptr || (cid & 255u) != 0 || (cid >> 8) >= 16) return;
-  const int w = threadIdx.x >> 5;
-  const unsigned k = atomicAdd(&g_trace_cnt[w], 1u);
-  if (k >= 1024) return;
-  unsigned long long* region =
-      reinterpret_cast<unsigned long long*>(err + 16) + ((cid >> 8) * 16 + w) * 2048;
-  long long clk;
-  asm volatile("mov.u64 %0, %%clock64;" : "=l"(clk));
-  region[2 * k] = (unsigned long long)clk;
-  region[2 * k + 1] = (unsigned long long)(ev | (j << 8) | (tile << 20) | (w << 24));
-}
-#define TRACE(ev, j, tile) trace_rec(args.err, ev, j, tile)
-__device__ int32_t* trace_err;
-#else
-#define TRACE(ev, j, tile) \
-  do {                     \
-  } while (0)
-#endif
-
-
-// P = 2^(S*scale_log2 - m) for one row of a 128-column tile, packed to bf16
-// pairs and stored to TMEM over the first 64 columns of the S tile; returns
-// the row sum of P (fp32). kPoly of every 8 column pairs use the FMA-pipe
-// exp2, the rest MUFU ex2 (the split is fixed at compile time so no path is
-// evaluated twice).
-template <int kPoly>
+// P = 2^(S*scale_log2 - m) for one row of a 128-column tile (MUFU ex2),
+// packed to bf16 pairs and stored to TMEM over the first 64 columns of the S
+// tile; returns the row sum of P (fp32).
 DLLM_DEVICE float exp_store_tile(const uint32_t (&s)[4][32], float sl2, float m, uint32_t tS) {
-  const f32x2_t sl2x2 = pk2(sl2, sl2);
-  const f32x2_t negm2 = pk2(-m, -m);
   const float neg_m = -m;
-  f32x2_t acc2 = pk2(0.f, 0.f);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t pk[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-      if ((e & 7) < kPoly) {
-        // FMA-pipe pair, packed f32x2 end to end
-        const f32x2_t x = ffma2(pk2u(s[c][2 * e], s[c][2 * e + 1]), sl2x2, negm2);
-        const f32x2_t p = exp2_poly2(x);
-        acc2 = fadd2(acc2, p);
-        float p0, p1;
-        upk2(p, p0, p1);
-        pk[e] = pack_bf16x2(p0, p1);
-      } else {
-        // MUFU pair with scalar arithmetic (no pair packing around MUFU)
-        const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
-        acc[(2 * e) & 3] += p0;
-        acc[(2 * e + 1) & 3] += p1;
-        pk[e] = pack_bf16x2(p0, p1);
-      }
+      const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
+      const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
+      acc[(2 * e) & 3] += p0;
+      acc[(2 * e + 1) & 3] += p1;
+      pk[e] = pack_bf16x2(p0, p1);
     }
     tmem_st16(tS + c * 16, pk);
-#ifdef DLLM_TRACE
-    if ((threadIdx.x & 127) == 0) trace_rec(trace_err, 17 + c, 0, 0);
-#endif
   }
-  float a0, a1;
-  upk2(acc2, a0, a1);
-  return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + (a0 + a1);
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
 }  // namespace
@@ -231,10 +179,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc + 16);
 
-#ifdef DLLM_TRACE
-  if (threadIdx.x < 16) g_trace_cnt[threadIdx.x] = 0;
-  if (threadIdx.x == 0) trace_err = args.err;
-#endif
   if (threadIdx.x == 0) {
     mbar_init(bar(BAR_Q), 1);
     mbar_init(bar(BAR_QEMPTY), 1);
@@ -297,7 +241,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     return u;
   };
-  if (threadIdx.x == 9 * 32) TRACE(1, 0, 0);
 
   if (warp == 8 || warp == 10) {
     // ------------------------------------------------------------------ TMA
@@ -419,7 +362,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(dk + kChunkBytes, mp, bar(bfull + st), 64, t.hkv, kt.row0, pol_kv);
         }
         ++done;
-        if (lane == 0) TRACE(kq ? 2 : 3, j, 0);
       }
     }
     if (lane == 0 && *abort_flag) {
@@ -486,7 +428,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st0 = kv_it % kStagesK;
           ok = mbar_wait(bar(BAR_KFULL + st0), (kv_it / kStagesK) & 1, abort_flag);
           if (!ok) break;
-          TRACE(4, 0, 0);
           tc_fence_after();
           const KvTile t0 = kv_tile(0, t.nc, t.c_begin, t.nk, t.k_begin);
           for (int i = 0; i < t.ntiles; ++i) {
@@ -502,7 +443,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const KvTile kt = kv_tile(j, t.nc, t.c_begin, t.nk, t.k_begin);
           ok = mbar_wait(bar(BAR_VFULL + vst), (kvj / kStagesV) & 1, abort_flag);
           if (!ok) break;
-          TRACE(5, j, 0);
           const bool more = j + 1 < t.nkv;
           const int kst = (kvj + 1) % kStagesK;
           const KvTile tn = more ? kv_tile(j + 1, t.nc, t.c_begin, t.nk, t.k_begin) : kt;
@@ -511,7 +451,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = mbar_wait(bar(BAR_PFULL + i), p_it[i] & 1, abort_flag);
             if (!ok) break;
             ++p_it[i];
-            TRACE(6, j, i);
             tc_fence_after();
             pv(i, vst, kt.valid, j > 0);
             if (more) {
@@ -526,7 +465,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               umma_commit(bar(BAR_OFULL + i));
             }
-            TRACE(7, j, i);
           }
           if (!ok) break;
           umma_commit(bar(BAR_VEMPTY + vst));
@@ -564,13 +502,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait_warp(bar(BAR_SFULL + wg), s_it & 1, abort_flag);
         if (!ok) break;
         ++s_it;
-        if (row_in_tile == 0) TRACE(10, j, wg);
         tc_fence_after();
         uint32_t s[4][32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
         tmem_wait_ld();
-        if (row_in_tile == 0) TRACE(11, j, wg);
         const bool partial = kt.valid < kTileN;
         if (partial) {
 #pragma unroll
@@ -590,7 +526,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mq[c] = fmaxf(a, __uint_as_float(s[c][31]));
         }
         const float mxs = max3f(mq[0], mq[1], fmaxf(mq[2], mq[3])) * sl2;
-        if (row_in_tile == 0) TRACE(16, j, wg);
         bool rescale = false;
         float alpha = 1.f;
         if (j == 0) {
@@ -608,14 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             rescale = true;
           }
         }
-        float rs;
-        if (partial) {
-          rs = exp_store_tile<0>(s, sl2, m, tS);  // masked columns: MUFU only (exact 0)
-        } else {
-          rs = exp_store_tile<kSmPoly>(s, sl2, m, tS);
-        }
-        if (row_in_tile == 0) TRACE(12, j, wg);
-        l += rs;
+        l += exp_store_tile(s, sl2, m, tS);  // masked columns give exact zeros
         if (rescale) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -631,7 +559,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(BAR_PFULL + wg));
-        if (row_in_tile == 0) TRACE(13, j, wg);
       }
       if (!ok) break;
       // Epilogue: O / l -> bf16 -> global.
@@ -643,7 +570,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait_warp(bar(BAR_OFULL + wg), o_it & 1, abort_flag);
         if (!ok) break;
         ++o_it;
-        if (row_in_tile == 0) TRACE(14, 0, wg);
         tc_fence_after();
         const float inv_l = 1.f / l;
         // Rows are spread one per lane; a 4x4 transpose of 16-byte vectors
@@ -689,7 +615,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (warp < 8 && row_in_tile_of(threadIdx.x) == 0) TRACE(15, 0, warp >> 2);
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {
@@ -716,7 +641,7 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, cons
                             const AttnKernelArgs& args, int max_q, int num_sms,
                             cudaStream_t stream) {
   // The smem opt-in is per device; remember it for up to 64 devices.
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;

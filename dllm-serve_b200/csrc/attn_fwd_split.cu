@@ -36,6 +36,8 @@
 //   segment 0: cached rows (k_cache/v_cache gathered rows, `cu_c`), optional
 //   segment 1: fresh rows of the step's k/v (`cu_k`)
 // KV tiles never straddle segments; a partial tile uses a smaller MMA N.
+#include <atomic>
+
 #include "common.cuh"
 #include "attn_fwd.h"
 
@@ -54,11 +56,6 @@ constexpr int kStagesV = 2;      // V ring depth
 constexpr int kThreads = 352;
 constexpr int kThreadsRope = 384;  // + the rotary warp
 
-// Softmax code-shape switch (tuning; default is the measured best).
-#ifndef DLLM_SM_POLY
-#define DLLM_SM_POLY 0
-#endif
-constexpr int kSmPoly = DLLM_SM_POLY;         // pairs of 8 evaluated on the FMA pipe
 constexpr uint32_t kTileBytes = kTileM * kD * 2;  // 32 KB (bf16)
 constexpr uint32_t kChunkBytes = 128 * 128;       // 128 rows x 128 B (64 bf16)
 
@@ -117,71 +114,26 @@ DLLM_DEVICE KvTile kv_tile(int t, int nc, int c0, int nk, int k0) {
   return r;
 }
 
-#ifdef DLLM_TRACE
-// Debug-only event trace (never built into the shipped library): for every
-// 256th CTA (up to 16) each warp records (clock64, code) pairs into its own
-// slice after the status word; per-warp counters live in shared memory.
-__shared__ unsigned g_trace_cnt[16];
-DLLM_DEVICE void trace_rec(int32_t* err, int ev, int j, int tile) {
-  const unsigned cid = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-  if (err == nullptr || (cid & 255u) != 0 || (cid >> 8) >= 16) return;
-  const int w = threadIdx.x >> 5;
-  const unsigned k = atomicAdd(&g_trace_cnt[w], 1u);
-  if (k >= 1024) return;
-  unsigned long long* region =
-      reinterpret_cast<unsigned long long*>(err + 16) + ((cid >> 8) * 16 + w) * 2048;
-  long long clk;
-  asm volatile("mov.u64 %0, %%clock64;" : "=l"(clk));
-  region[2 * k] = (unsigned long long)clk;
-  region[2 * k + 1] = (unsigned long long)(ev | (j << 8) | (tile << 20) | (w << 24));
-}
-#define TRACE(ev, j, tile) trace_rec(args.err, ev, j, tile)
-__device__ int32_t* trace_err;
-#else
-#define TRACE(ev, j, tile) \
-  do {                     \
-  } while (0)
-#endif
-
-
-
 // P = 2^(S*scale_log2 - m) for one row of a 64-column half tile (two chunks
-// of 32 columns), packed to bf16 pairs and stored to TMEM at tP (chunk c ->
-// columns 16c .. 16c+15); returns the row sum of P (fp32). kPoly of every 8
-// column pairs use the FMA-pipe exp2, the rest MUFU ex2 (the split is fixed
-// at compile time so no path is evaluated twice).
-template <int kPoly>
+// of 32 columns, MUFU ex2), packed to bf16 pairs and stored to TMEM at tP
+// (chunk c -> columns 16c .. 16c+15); returns the row sum of P (fp32).
 DLLM_DEVICE float exp_store_half(const uint32_t (&s)[2][32], float sl2, float m, uint32_t tP) {
-  const f32x2_t sl2x2 = pk2(sl2, sl2);
-  const f32x2_t negm2 = pk2(-m, -m);
   const float neg_m = -m;
-  f32x2_t acc2 = pk2(0.f, 0.f);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     uint32_t pk[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-      if ((e & 7) < kPoly) {
-        const f32x2_t x = ffma2(pk2u(s[c][2 * e], s[c][2 * e + 1]), sl2x2, negm2);
-        const f32x2_t p = exp2_poly2(x);
-        acc2 = fadd2(acc2, p);
-        float p0, p1;
-        upk2(p, p0, p1);
-        pk[e] = pack_bf16x2(p0, p1);
-      } else {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
-        acc[(2 * e) & 3] += p0;
-        acc[(2 * e + 1) & 3] += p1;
-        pk[e] = pack_bf16x2(p0, p1);
-      }
+      const float p0 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
+      const float p1 = ex2_approx(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
+      acc[(2 * e) & 3] += p0;
+      acc[(2 * e + 1) & 3] += p1;
+      pk[e] = pack_bf16x2(p0, p1);
     }
     tmem_st16(tP + c * 16, pk);
   }
-  float a0, a1;
-  upk2(acc2, a0, a1);
-  return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + (a0 + a1);
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
 }  // namespace
@@ -329,10 +281,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc + 16);
 
-#ifdef DLLM_TRACE
-  if (threadIdx.x < 16) g_trace_cnt[threadIdx.x] = 0;
-  if (threadIdx.x == 0) trace_err = args.err;
-#endif
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStagesQ; ++s) {
       mbar_init(bar(BAR_QFULL + s), 1);
@@ -384,7 +332,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
   // previous kernel in the stream; every global access below comes after it.
   griddep_wait();
   griddep_launch_dependents();
-  if (threadIdx.x == 9 * 32) TRACE(1, 0, 0);
 
   if (warp == 8 || warp == 10) {
     // ------------------------------------------------------------------ TMA
@@ -494,7 +441,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
           }
         }
         ++done;
-        if (lane == 0) TRACE(kq ? 2 : 3, j, 0);
       }
     }
     if (lane == 0 && *abort_flag) {
@@ -611,7 +557,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
           if (!ok) break;
           ok = mbar_wait(bar(BAR_PFULL + sb), (g >> 1) & 1, abort_flag);
           if (!ok) break;
-          TRACE(6, j, 0);
           tc_fence_after();
           const int ks = (kt.valid + 15) >> 4;  // 1..8 K-steps
           pv_half(vst, sb, 0, ks < 4 ? ks : 4, j > 0);
@@ -634,7 +579,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
             ++k_it;
             if (j + 3 == t.nkv) umma_commit(bar(BAR_QEMPTY + qs));  // last QK issued
           }
-          TRACE(7, j, 0);
         }
         if (!ok) break;
         umma_commit(bar(BAR_OFULL));
@@ -708,7 +652,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
         const uint32_t sb = g & 1;
         ok = mbar_wait_warp(bar(BAR_SFULL + sb), (g >> 1) & 1, abort_flag);
         if (!ok) break;
-        if (row_in_tile == 0) TRACE(10, j, wg);
         tc_fence_after();
         const uint32_t tS = tmem + lane_base + sb * 128 + wg * kHalfN;
         int nv = kt.valid - wg * kHalfN;  // valid columns of this half (warp-uniform)
@@ -765,19 +708,12 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
               }
             }
           }
-          float rs;
-          if (nv < kHalfN) {
-            rs = exp_store_half<0>(s, sl2, m, tS);  // masked columns: MUFU only (exact 0)
-          } else {
-            rs = exp_store_half<kSmPoly>(s, sl2, m, tS);
-          }
-          l += rs;
+          l += exp_store_half(s, sl2, m, tS);  // masked columns give exact zeros
           tmem_wait_st();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(BAR_PFULL + sb));
-        if (row_in_tile == 0) TRACE(13, j, wg);
       }
       if (!ok) break;
       // Epilogue: merge the two halves, O / l -> bf16 -> global. Warpgroup w
@@ -821,7 +757,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
           mbar_arrive(bar(BAR_XF));
         }
         ++o_it;
-        if (row_in_tile == 0) TRACE(14, 0, wg);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t oa[32], ob[32];
@@ -861,7 +796,6 @@ __global__ void __launch_bounds__(kRope ? kThreadsRope : kThreads, 1)
     }
   }
 
-  if (warp < 8 && row_in_tile_of(threadIdx.x) == 0) TRACE(15, 0, warp >> 2);
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {
@@ -878,7 +812,7 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
                             const AttnKernelArgs& args, int max_q, int num_sms,
                             cudaStream_t stream) {
   // The smem opt-in is per device and instantiation; remember it for up to 64 devices.
-  static bool attr_set[2][64] = {{false}};
+  static std::atomic<bool> attr_set[2][64];
   const bool rope = args.positions != nullptr;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -1,5 +1,6 @@
 // extern "C" entry points of libdllm_attn.so (declared in include/dllm_attn.h):
 // argument validation, TMA tensor-map encoding and kernel dispatch.
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -33,17 +34,19 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// SM count per device, queried once (host threads racing on the first query
+// store the same value).
 int num_sms_of_current_device() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
       n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
@@ -249,17 +252,20 @@ constexpr int kStaticWsInts = 64;
 static __device__ __align__(256) int32_t g_static_sched_ws[kStaticWsInts];
 
 // Device address of g_static_sched_ws on the current device, looked up once
-// per device; nullptr (and the CUDA error in *e) if the lookup fails.
-int32_t* static_sched_ws(cudaError_t* e) {
-  static int32_t* addr[64] = {nullptr};
-  int dev = 0;
-  *e = cudaGetDevice(&dev);
-  if (*e != cudaSuccess) return nullptr;
-  if (dev >= 0 && dev < 64 && addr[dev] != nullptr) return addr[dev];
+// per device (host threads racing on the first lookup store the same value);
+// nullptr (and the CUDA error in *e) if the lookup fails. The address stays
+// valid until the device's context is destroyed (cudaDeviceReset, process exit).
+int32_t* static_sched_ws(int dev, cudaError_t* e) {
+  static std::atomic<int32_t*> addr[64];
+  *e = cudaSuccess;
+  if (dev >= 0 && dev < 64) {
+    int32_t* p = addr[dev].load(std::memory_order_acquire);
+    if (p != nullptr) return p;
+  }
   void* p = nullptr;
   *e = cudaGetSymbolAddress(&p, g_static_sched_ws);
   if (*e != cudaSuccess) return nullptr;
-  if (dev >= 0 && dev < 64) addr[dev] = static_cast<int32_t*>(p);
+  if (dev >= 0 && dev < 64) addr[dev].store(static_cast<int32_t*>(p), std::memory_order_release);
   return static_cast<int32_t*>(p);
 }
 
@@ -310,8 +316,18 @@ int dllm_attn_varlen_fwd_static_ws(const void* q, int64_t q_tok_stride, const vo
   if (DLLM_SCHED_WORKSPACE_INTS > kStaticWsInts)
     return fail(DLLM_ERR_TOO_LARGE, "scheduler workspace needs %d words > %d", DLLM_SCHED_WORKSPACE_INTS,
                 kStaticWsInts);
-  cudaError_t e = cudaSuccess;
-  int32_t* ws = static_sched_ws(&e);
+  // The array lives on the current device; a stream of another device would
+  // run the kernel there with this device's address.
+  int dev = 0, stream_dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &stream_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamGetDevice");
+  if (stream_dev != dev)
+    return fail(DLLM_ERR_INVALID_ARG,
+                "stream belongs to device %d but device %d is current; make the stream's device current",
+                stream_dev, dev);
+  int32_t* ws = static_sched_ws(dev, &e);
   if (ws == nullptr) return cuda_fail(e, "cudaGetSymbolAddress(static scheduler workspace)");
   return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, nullptr, 0, nullptr, 0, o,
                      o_tok_stride, cu_seqlens_q, cu_seqlens_k, nullptr, batch, max_seqlen_q,

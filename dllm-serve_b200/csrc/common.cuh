@@ -412,70 +412,4 @@ DLLM_DEVICE void rope_rotate8(uint4& w1, uint4& w2, const float (&c)[8], const f
   w2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
 }
 
-
-// Packed two-lane fp32 arithmetic (Blackwell f32x2). A pair lives in one
-// 64-bit register (low half = first element) so chains of pair operations
-// need no repacking.
-typedef unsigned long long f32x2_t;
-
-DLLM_DEVICE f32x2_t pk2(float lo, float hi) {
-  f32x2_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-DLLM_DEVICE f32x2_t pk2u(uint32_t lo, uint32_t hi) {
-  f32x2_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-  return r;
-}
-DLLM_DEVICE void upk2(f32x2_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-DLLM_DEVICE f32x2_t ffma2(f32x2_t a, f32x2_t b, f32x2_t c) {  // a * b + c
-  f32x2_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-DLLM_DEVICE f32x2_t fadd2(f32x2_t a, f32x2_t b) {
-  f32x2_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-DLLM_DEVICE f32x2_t fmul2(f32x2_t a, f32x2_t b) {
-  f32x2_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// 2^x on the FMA pipe for a pair (x <= ~126). Cody-Waite style range
-// reduction x = n + f, n = nearest integer (via the 1.5*2^23 rounding
-// constant), f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients
-// were fitted for this library (iteratively reweighted least squares on
-// Chebyshev nodes, max relative error 7.5e-5 - far below bf16's 2^-9);
-// 2^n is applied by adding n to the exponent field. Inputs below -125 are
-// clamped there (result ~2e-38 instead of 0), so callers keep masked (-inf)
-// columns on the MUFU path.
-constexpr float kExp2C0 = 0.9999280571937561f;
-constexpr float kExp2C1 = 0.6932609677314758f;
-constexpr float kExp2C2 = 0.2426111400127411f;
-constexpr float kExp2C3 = 0.0551716573536396f;
-constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
-
-DLLM_DEVICE f32x2_t exp2_poly2(f32x2_t x) {
-  float x0, x1;
-  upk2(x, x0, x1);
-  x = pk2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-  const f32x2_t t = fadd2(x, pk2(kRoundMagic, kRoundMagic));
-  const f32x2_t n = fadd2(t, pk2(-kRoundMagic, -kRoundMagic));
-  const f32x2_t f = ffma2(n, pk2(-1.f, -1.f), x);
-  f32x2_t p = ffma2(pk2(kExp2C3, kExp2C3), f, pk2(kExp2C2, kExp2C2));
-  p = ffma2(p, f, pk2(kExp2C1, kExp2C1));
-  p = ffma2(p, f, pk2(kExp2C0, kExp2C0));
-  float p0, p1, t0, t1;
-  upk2(p, p0, p1);
-  upk2(t, t0, t1);
-  return pk2(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
-             __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
-}
-
 }  // namespace dllm

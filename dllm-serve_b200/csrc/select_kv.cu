@@ -17,6 +17,10 @@
 // is "descending score, ties by ascending candidate index".
 #include <cooperative_groups.h>
 
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
 #include "common.cuh"
 #include "select_kv.h"
 
@@ -419,18 +423,23 @@ cudaError_t launch_select_kv(const SelectArgs& a, bool head_select, int n_seqs, 
   // The dynamic-smem opt-in is per device and kernel; raise it only when a
   // launch needs more than before (so steady-state launches, including ones
   // recorded into a CUDA graph, make no attribute calls).
-  static size_t smem_set[2][64] = {{0}};
+  // Host threads share these caches; raising the attribute is serialised so
+  // that a concurrent smaller request never lowers it under a larger one.
+  static std::atomic<size_t> smem_set[2][64];
+  static std::mutex raise_mu;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  size_t* have = (dev >= 0 && dev < 64) ? &smem_set[head_select ? 1 : 0][dev] : nullptr;
-  if (have == nullptr || *have < smem) {
+  std::atomic<size_t>* have = (dev >= 0 && dev < 64) ? &smem_set[head_select ? 1 : 0][dev] : nullptr;
+  if (have == nullptr || have->load(std::memory_order_acquire) < smem) {
+    std::lock_guard<std::mutex> lock(raise_mu);
+    const size_t target = have != nullptr ? std::max(have->load(), smem) : smem;
     e = head_select ? cudaFuncSetAttribute(select_kv_kernel<true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)target)
                     : cudaFuncSetAttribute(select_kv_kernel<false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)target);
     if (e != cudaSuccess) return e;
-    if (have != nullptr) *have = smem;
+    if (have != nullptr) have->store(target, std::memory_order_release);
   }
   if (head_select)
     return launch_pdl(select_kv_kernel<true>, grid, dim3(kThreads), smem, stream, a);

@@ -35,8 +35,8 @@
  *     device pointer owned by the caller. The library never allocates or frees memory,
  *     never synchronises the stream and never reads device data on the host, so a call
  *     of any entry point that works only on caller buffers can be captured in a CUDA
- *     graph (dllm_attn_varlen_fwd_static_ws, which uses a library array, is not one of
- *     them).
+ *     graph (this statement does not cover dllm_attn_varlen_fwd_static_ws, whose
+ *     workspace is a library array).
  *   - `stream` is a cudaStream_t passed as void*. NULL means the legacy default stream.
  *   - Strides are in ELEMENTS unless the name ends in `_bytes`.
  *   - bf16 tensors are laid out [tokens, heads, head_dim] with head_dim contiguous and
@@ -132,15 +132,27 @@ DLLM_API int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const voi
                          int32_t* sched_workspace, int32_t* err_flag, void* stream);
 
 /*
- * dllm_attn_varlen_fwd with its scheduler workspace taken from memory the library
- * owns: a file-scope static device array of 64 int32 words (one per device, zero
- * when the library loads; the call uses the first DLLM_SCHED_WORKSPACE_INTS and the
- * kernel returns them to zero on exit). Allocates nothing; the array's address is
- * looked up once per device with cudaGetSymbolAddress (the device current at the
- * call). Returns DLLM_ERR_TOO_LARGE if a workspace would not fit the array.
- * Calls that overlap in time on one device (several streams or threads) share
- * the words and race: run them one after another. No reference counterpart: the
- * reference's flash_attn_varlen_func has no scheduler workspace.
+ * dllm_attn_varlen_fwd for callers that cannot allocate device memory. It
+ * allocates nothing: the scheduler workspace that dllm_attn_varlen_fwd takes
+ * from the caller lives instead in a file-scope static device array of the
+ * library, 64 int32 words per device (every device that loads the library
+ * holds it until the process exits; the call uses the first
+ * DLLM_SCHED_WORKSPACE_INTS words and returns DLLM_ERR_TOO_LARGE if a
+ * workspace would not fit). Typical callers: a plugin whose host application
+ * owns all device memory through its own pool and hands it only input/output
+ * pointers, and launch loops that must not call cudaMalloc, which can
+ * synchronise the device and would stall the stream they are feeding.
+ * The caller still passes every input and output.
+ *
+ * Set-up: the first call on a device (with that device current) looks up the
+ * array's device address with cudaGetSymbolAddress and keeps it for later
+ * calls; make that first call before any stream capture. The stream must
+ * belong to the current device (DLLM_ERR_INVALID_ARG otherwise). The kernel
+ * leaves the words at zero on every exit path, so each call starts from a
+ * clean state; calls that overlap in time on one device (several streams or
+ * host threads) share the words and race: run them one after another.
+ * No counterpart in the reference (its flash_attn_varlen_func takes no
+ * workspace).
  */
 DLLM_API int dllm_attn_varlen_fwd_static_ws(const void* q, int64_t q_tok_stride, const void* k,
                                    int64_t k_tok_stride, const void* v, int64_t v_tok_stride,

@@ -29,8 +29,10 @@ import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 import cases as C  # noqa: E402
 import inputs as I  # noqa: E402
+from oracle import reference_module as RM  # noqa: E402
 
 
 class _TorchProxy:
@@ -47,49 +49,10 @@ class _TorchProxy:
         return r
 
 
-def _flash_stub(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q=0, max_seqlen_k=0,
-                softmax_scale=None, causal=False, **_):
-    assert not causal
-    out = torch.zeros(q.shape, dtype=torch.float32)
-    cq, ck = cu_seqlens_q.tolist(), cu_seqlens_k.tolist()
-    for b in range(len(cq) - 1):
-        qs, ks, vs = q[cq[b]:cq[b + 1]], k[ck[b]:ck[b + 1]], v[ck[b]:ck[b + 1]]
-        if qs.shape[0] == 0:
-            continue
-        rep = qs.shape[1] // ks.shape[1]
-        ks, vs = ks.repeat_interleave(rep, 1), vs.repeat_interleave(rep, 1)
-        o = F.scaled_dot_product_attention(qs.transpose(0, 1).float(), ks.transpose(0, 1).float(),
-                                           vs.transpose(0, 1).float(), scale=softmax_scale)
-        out[cq[b]:cq[b + 1]] = o.transpose(0, 1)
-    return out
-
-
-def _store_stub(key, value, k_cache, v_cache, slot_mapping):
-    N, H, Dh = key.shape
-    assert slot_mapping.numel() == N
-    k_cache.view(-1, H * Dh)[slot_mapping.long()] = key.reshape(N, -1)
-    v_cache.view(-1, H * Dh)[slot_mapping.long()] = value.reshape(N, -1)
-
-
-def _load_stub(key, value, k_cache, v_cache, slot_mapping):
-    N, H, Dh = key.shape
-    assert slot_mapping.numel() == N
-    key.copy_(k_cache.view(-1, H * Dh)[slot_mapping.long()].view(N, H, Dh))
-    value.copy_(v_cache.view(-1, H * Dh)[slot_mapping.long()].view(N, H, Dh))
-
-
 def load_reference(path):
-    sys.path.insert(0, path)
-    import dllmserve.layers.attention as att
-    import dllmserve.utils.context as ctx
-    from dllmserve.engine.sequence import Sequence
-    from dllmserve.sparse.state import SparseConfig
-    from dllmserve.layers.rotary_embedding import RotaryEmbedding, apply_rotary_emb
-    att.flash_attn_varlen_func = _flash_stub
-    att.store_kvcache = _store_stub
-    att.load_kvcache = _load_stub
-    return types.SimpleNamespace(att=att, ctx=ctx, Sequence=Sequence, SparseConfig=SparseConfig,
-                                 RotaryEmbedding=RotaryEmbedding, apply_rotary_emb=apply_rotary_emb)
+    """The reference's attention module with CPU stand-ins for its flash-attn
+    and Triton callees (oracle/reference_module.py)."""
+    return RM.load(path)
 
 
 def _fake_config():
