@@ -70,7 +70,10 @@ def use_context(ctx: Context) -> None:
     per-step device metadata on the Context, so reinstalling the same object
     for steps with identical sequence states (e.g. the reuse steps of a
     diffusion block) skips rebuilding it and keeps CUDA-graph captures free of
-    host-to-device copies."""
+    host-to-device copies. A CUDA graph captured under a Context reads that
+    metadata (sequence offsets, selection descriptors, slot lists) by device
+    address: keep the Context object alive, and unchanged, for as long as the
+    graph is replayed."""
     global _CONTEXT
     _CONTEXT = ctx
 

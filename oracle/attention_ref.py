@@ -133,6 +133,126 @@ def shared_scores(q_block, k_cand, num_heads, num_kv_heads) -> np.ndarray:
     return _div_sqrt_d(s.astype(np.float32), D)
 
 
+# ---------------------------------------------------------------------------
+# The same scores in the fp32 accumulation order of the GPU selection kernel
+# (dllm-serve_b200/csrc/select_kv.cu). The reference fixes no summation order
+# (it scores in bf16 on the GPU, fp32 on the CPU); restating the kernel's order
+# makes scores -- and with them the top-k indices -- bit-identical on ANY
+# input, so selection can be checked bit for bit on plain N(0,1) data at full
+# size. Parity with the reference's own ordering is pinned separately, on
+# margin-separated inputs where every summation order ranks alike.
+# ---------------------------------------------------------------------------
+def fma32(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
+    """fp32 fused multiply-add with one rounding (round to nearest even).
+    The product of two fp32 values is exact in float64; the float64 sum's
+    rounding error is recovered exactly (TwoSum), and the one case where
+    rounding float64 -> fp32 can then differ from a single rounding (the
+    float64 sum sits exactly halfway between two fp32 values) is corrected by
+    the error's sign."""
+    a64, b64, c64 = (np.asarray(x, dtype=np.float32).astype(np.float64) for x in (a, b, c))
+    p = a64 * b64
+    s = p + c64
+    bv = s - p
+    e = (p - (s - bv)) + (c64 - bv)
+    r = s.astype(np.float32)
+    r64 = r.astype(np.float64)
+    toward = np.where(s > r64, np.float32(np.inf), np.float32(-np.inf)).astype(np.float32)
+    other = np.nextafter(r, toward)
+    mid = (r64 + other.astype(np.float64)) * 0.5
+    tie = (s != r64) & (s == mid) & (e != 0) & (np.sign(e) == np.sign(s - r64))
+    return np.where(tie, other, r).astype(np.float32)
+
+
+def q_block_mean_kernel_order(q_block: torch.Tensor) -> np.ndarray:
+    """q_block.mean(dim=0) as the kernel sums it: eight interleaved fp32
+    partial sums (row t into partial t mod 8, rows in increasing order; rows
+    past the last multiple of 8 into partial 0), combined as
+    ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)), then an fp32 division by the row count."""
+    qb = q_block.float().numpy().astype(np.float32)
+    n = qb.shape[0]
+    s8 = np.zeros((8,) + qb.shape[1:], dtype=np.float32)
+    t = 0
+    while t + 8 <= n:
+        for u in range(8):
+            s8[u] = s8[u] + qb[t + u]
+        t += 8
+    while t < n:
+        s8[0] = s8[0] + qb[t]
+        t += 1
+    tot = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))
+    return (tot / np.float32(n)).astype(np.float32)
+
+
+def _xor_tree_sum(v: np.ndarray) -> np.ndarray:
+    """Butterfly sum over the last axis (lanes): v_l += v_(l xor o) for
+    o = n/2, ..., 1; every lane ends with the same value, returned."""
+    n = v.shape[-1]
+    lanes = np.arange(n)
+    o = n // 2
+    while o >= 1:
+        v = (v + v[..., lanes ^ o]).astype(np.float32)
+        o //= 2
+    return v[..., 0]
+
+
+def head_scores_kernel_order(q_block, k_cand, num_heads, num_kv_heads) -> np.ndarray:
+    """head_scores() in the kernel's order: 16 lanes x 8 dims per candidate row;
+    per lane the product of dims 8l and then an FMA chain over the next 7,
+    a 16-lane butterfly sum, max over the GQA group, fp32 division by
+    fp32(sqrt(D))."""
+    D = q_block.shape[2]
+    G = num_heads // num_kv_heads
+    q_avg = q_block_mean_kernel_order(q_block).reshape(num_kv_heads, G, 16, 8)   # [Hkv,G,lane,i]
+    kp = k_cand.float().numpy().astype(np.float32).transpose(1, 0, 2)           # [Hkv,Klen,D]
+    kl = kp.reshape(num_kv_heads, 1, kp.shape[1], 16, 8)                        # [Hkv,1,Klen,lane,i]
+    qa = q_avg[:, :, None, :, :]                                                # [Hkv,G,1,lane,i]
+    p = (qa[..., 0] * kl[..., 0]).astype(np.float32)
+    for i in range(1, 8):
+        p = fma32(qa[..., i], kl[..., i], p)
+    s = _xor_tree_sum(p)                                                        # [Hkv,G,Klen]
+    s = s.max(axis=1)
+    return (s / np.float32(math.sqrt(D))).astype(np.float32)
+
+
+def shared_scores_kernel_order(q_block, k_cand, num_heads, num_kv_heads) -> np.ndarray:
+    """shared_scores() in the kernel's order: a warp per candidate row, lane l
+    taking the 8-element vectors e = l, l + 32, ... of the row (vector e is
+    dims 8(e mod 16).. of KV head e div 16) and, for each, one FMA chain over
+    the group's query heads then the 8 dims; a 32-lane butterfly sum; fp32
+    division by fp32(sqrt(D))."""
+    D = q_block.shape[2]
+    G = num_heads // num_kv_heads
+    q_avg = q_block_mean_kernel_order(q_block)                                  # [Hq, D]
+    kc = k_cand.float().numpy().astype(np.float32).reshape(k_cand.shape[0], -1)  # [Klen, Hkv*D]
+    row_vec = num_kv_heads * D // 8
+    klen = kc.shape[0]
+    p = np.zeros((klen, 32), dtype=np.float32)
+    for e0 in range(0, row_vec, 32):
+        lanes = np.arange(32)
+        e = e0 + lanes
+        valid = e < row_vec
+        hk, dd = (e * 8) // D, (e * 8) % D
+        for g in range(G):
+            for i in range(8):
+                qv = np.where(valid, q_avg[np.minimum(hk * G + g, num_heads - 1), np.minimum(dd + i, D - 1)],
+                              np.float32(0))
+                xv = kc[:, np.minimum(e * 8 + i, kc.shape[1] - 1)]                # [Klen, 32]
+                nxt = fma32(qv[None, :], xv, p)
+                p = np.where(valid[None, :], nxt, p)
+    s = _xor_tree_sum(p)
+    return (s / np.float32(math.sqrt(D))).astype(np.float32)
+
+
+def select_kernel_order(q_block, k_cand, num_heads, num_kv_heads, pool_kernel, ratio, head_select):
+    """top-k indices of the kernel-order scores: [Hkv, n_keep] with
+    head_select, else [n_keep]."""
+    if head_select:
+        s = head_scores_kernel_order(q_block, k_cand, num_heads, num_kv_heads)
+    else:
+        s = shared_scores_kernel_order(q_block, k_cand, num_heads, num_kv_heads)
+    return topk_desc(max_pool(s, pool_kernel), num_keep(k_cand.shape[0], ratio))
+
+
 def max_pool(scores: np.ndarray, pool_kernel: int) -> np.ndarray:
     """F.max_pool1d(kernel=pool_kernel, stride=1, padding=pool_kernel//2)[..., :Klen]
     along the last axis, padding acting as -inf (attention.py:386-393, :328-335)."""

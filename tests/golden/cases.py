@@ -70,3 +70,32 @@ STATE_TRACES = [
     (3, 8, 0, 20, 30),
     (1, 32, 7, 0, 5),
 ]
+
+
+# Selection at benchmark scale (BASELINE configs 3 and 4), one compute-cache
+# step per sequence at its first generation block. Inputs: N(0,1) q/k/v with
+# margin-separated keys (inputs.margin_selection_batch), so every fp32
+# summation order ranks the candidates alike and the reference's top_idx can
+# be matched index for index. Only top_idx is recorded (the outputs at this
+# size are checked against the oracle on the GPU instead).
+@dataclass
+class SelectionCase:
+    name: str
+    seed: int
+    num_heads: int
+    num_kv_heads: int
+    batch: int
+    prompt_range: tuple
+    gen_len: int
+    head_select: bool
+    retention_ratio: float = 0.5
+    pool_kernel: int = 3
+    block_len: int = 32
+    scaled_heads: int = 0        # KV heads whose keys are scaled 3x (config 3's recipe)
+
+
+SELECTION_CASES = [
+    SelectionCase("c3_sel", 3, 32, 32, 8, (512, 512), 128, True, scaled_heads=4),
+    SelectionCase("c4_sel_head", 4, 28, 4, 32, (128, 768), 256, True),
+    SelectionCase("c4_sel_shared", 5, 28, 4, 32, (128, 768), 256, False),
+]

@@ -146,6 +146,42 @@ def make_sparse_case(R, case: C.SparseCase):
     return res, meta
 
 
+def make_selection_case(R, case: C.SelectionCase):
+    """One compute-cache (state 1) step of the reference's Attention.forward
+    on a SelectionCase batch (inputs.margin_selection_batch); records the
+    reference's top_idx of every sequence (its torch.topk indices)."""
+    H, Hk, Dh, blk = case.num_heads, case.num_kv_heads, 128, case.block_len
+    q, k, v, prompts, lens = I.margin_selection_batch(case)
+    cfg = R.SparseConfig(enabled=True, default_block_len=blk, retention_ratio=case.retention_ratio,
+                         pool_kernel=case.pool_kernel, delay_step=1, head_select=case.head_select)
+    seqs, slots, page = [], [], 0
+    for p in prompts:
+        s = R.Sequence([1] * p, types.SimpleNamespace(gen_length=case.gen_len), _fake_config(), cfg)
+        s.sparse_state.current_block_idx = 0
+        s.sparse_state.cache_state = 1
+        n = s.current_sparse_token
+        npg = (n + 255) // 256
+        slots.append(torch.arange(page * 256, page * 256 + n, dtype=torch.int32))
+        page += npg
+        seqs.append(s)
+    layer = R.att.Attention(H, Dh, Dh ** -0.5, Hk, causal=False)
+    layer.k_cache = torch.zeros(page, 256, Hk, Dh)
+    layer.v_cache = torch.zeros(page, 256, Hk, Dh)
+    log = []
+    R.att.torch = _TorchProxy(torch, log)
+    try:
+        _run_layer(R, layer, q, k, v, seqs, slots)
+    finally:
+        R.att.torch = torch
+    assert len(log) == len(seqs), (len(log), len(seqs))
+    res = {"input_checksums": np.array(I.checksum(q) + I.checksum(k) + I.checksum(v)),
+           "lens": np.array(lens, np.int32),
+           "n_keep": np.array([s.current_sparse_token for s in seqs], np.int32)}
+    for i, idx in enumerate(log):
+        res[f"top_idx_{i}"] = idx.numpy().astype(np.int16)
+    return res
+
+
 def make_c1(R):
     c = C.C1
     g = I.gen(c["seed"])
@@ -195,6 +231,8 @@ def main():
     R = load_reference(args.reference)
     meta = {"torch": torch.__version__, "cases": {}}
     np.savez_compressed(os.path.join(HERE, "c1.npz"), **make_c1(R))
+    for case in C.SELECTION_CASES:
+        np.savez_compressed(os.path.join(HERE, f"selection_{case.name}.npz"), **make_selection_case(R, case))
     for case in C.SPARSE_CASES:
         res, m = make_sparse_case(R, case)
         np.savez_compressed(os.path.join(HERE, f"sparse_{case.name}.npz"), **res)

@@ -4,6 +4,8 @@ Tolerances (from the benchmark spec): attention outputs in bf16 vs the fp32
 oracle within max-abs 2e-2 and mean-abs 2e-3; KV-cache contents bit-exact;
 selected indices bit-exact (same tie rule: descending score, ascending index).
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -331,9 +333,10 @@ def test_attention_single_tile_segments(dev, case, hq, hkv):
     _status_clear(dev)
 
 
-def test_attention_c2_full_size_sampled(dev):
-    """Config-2 shapes (B=16, L in [384,1152], 32 MHA heads): every output
-    row finite; a sample of (sequence, head) pairs checked against the oracle."""
+def test_attention_c2_full_layer(dev):
+    """A whole config-2 layer (B=16, L in [419, 1087], 32 MHA heads, 157.6
+    GFLOP): every (sequence, head) pair against the fp32 oracle, each within
+    max-abs 2e-2 / mean-abs 2e-3."""
     import bench
 
     lens = bench.workload_lengths()
@@ -347,13 +350,16 @@ def test_attention_c2_full_size_sampled(dev):
     cud = torch.tensor(cu, dtype=torch.int32, device=dev)
     out = _ops().varlen_attention(q, k, v, cud, cud, max(lens))
     torch.cuda.synchronize()
-    assert torch.isfinite(out.float()).all()
-    for b in (0, 7, 15):
-        for h in (0, 13, 31):
-            s0, s1 = cu[b], cu[b + 1]
-            ref = R.sdpa_seq(q[s0:s1, h:h + 1].cpu(), k[s0:s1, h:h + 1].cpu(),
-                             v[s0:s1, h:h + 1].cpu(), D ** -0.5)
-            _check_attn(out[s0:s1, h:h + 1], ref, f"seq {b} head {h}")
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    ref = R.varlen_attention(q.float().cpu(), k.float().cpu(), v.float().cpu(), cu, cu, D ** -0.5)
+    err = (out.float().cpu() - ref).abs()
+    worst_max = worst_mean = 0.0
+    for b in range(len(lens)):
+        e = err[cu[b]:cu[b + 1]]                      # [L, H, D]
+        mx = e.amax(dim=(0, 2))
+        mean = e.mean(dim=(0, 2))
+        worst_max, worst_mean = max(worst_max, float(mx.max())), max(worst_mean, float(mean.max()))
+    assert worst_max <= 2e-2 and worst_mean <= 2e-3, (worst_max, worst_mean)
     _status_clear(dev)
 
 
