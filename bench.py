@@ -534,6 +534,11 @@ def run_ours(args, lens):
                                 "(cuBLAS, bf16) + NCCL all-reduce of [tokens, 4096] bf16",
                     "steps": steps_tp}
 
+    # ---------------- config-3 sparse diffusion block (r=0.5, head_select) ----------------
+    sparse_block = None
+    if not args.skip_extras:
+        sparse_block = sparse_cycle("c3", args.steps, args.warmup)
+
     # ---------------- e2e through the public API, host buffers ----------------
     e2e = None
     if not args.skip_extras:
@@ -624,7 +629,7 @@ def run_ours(args, lens):
             "step_tokens_per_s": tokens_per_s,
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": launches, "kv_store": kv_block, "rope": rope_block,
-            "rope_fused_reuse": rope_fused, "tp_layer": tp_block,
+            "rope_fused_reuse": rope_fused, "tp_layer": tp_block, "sparse_cycle_c3": sparse_block,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -648,11 +653,33 @@ SPARSE_WORKLOADS = {
 
 
 def run_sparse_cycle(args):
+    """``--workload c3|c4|c5``: prints the sparse_cycle() line of the workload."""
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    line = sparse_cycle(args.workload, args.steps, args.warmup)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    return 0
+
+
+def sparse_cycle(workload, steps, warmup):
     """One diffusion block = 32 denoising steps with SparseConfig(delay_step=1,
     block 32): state 0 (dense), state 1 (dense + select/store), 30 x state 2
-    (block queries over cached + fresh keys), timed against 32 dense steps.
-    Every layer is the public Attention module driven through set_context,
-    as the model runner drives it; q/k/v are synthetic per layer."""
+    (block queries over cached + fresh keys), timed against 32 dense steps,
+    eagerly (each step builds a new Context and launches from Python, as the
+    reference's model runner does) and as per-state CUDA graphs. Every layer
+    is the public Attention module; q/k/v are synthetic per layer. Runs on
+    this rank's head slice under an initialised process group."""
     import torch.distributed as dist
 
     from dllmserve_b200 import _native, ops
@@ -661,18 +688,15 @@ def run_sparse_cycle(args):
     from dllmserve_b200.tp import head_slice
     from dllmserve_b200.utils.context import reset_context, set_context
 
-    layers, Hq_all, Hkv_all, B, (plo, phi), gen, ratio, desc = SPARSE_WORKLOADS[args.workload]
+    layers, Hq_all, Hkv_all, B, (plo, phi), gen, ratio, desc = SPARSE_WORKLOADS[workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     _native.lib()
     h0, h1, k0, k1 = head_slice(Hq_all, Hkv_all, rank, world)
     Hq, Hkv = h1 - h0, k1 - k0
-    g = torch.Generator().manual_seed(40 + int(args.workload[1]))
+    g = torch.Generator().manual_seed(40 + int(workload[1]))
     prompts = torch.randint(plo, phi + 1, (B,), generator=g).tolist()
     lens = [p + gen for p in prompts]
     blk = 32
@@ -750,9 +774,9 @@ def run_sparse_cycle(args):
         return ms
 
     dense_seqs = [Seq(p, L, False) for p, L in zip(prompts, lens)]
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         step(dense_seqs)
-    dense_ms = timed(lambda: step(dense_seqs), max(1, min(args.steps, 10)))
+    dense_ms = timed(lambda: step(dense_seqs), max(1, min(steps, 10)))
 
     sparse_seqs = [Seq(p, L, True) for p, L in zip(prompts, lens)]
 
@@ -768,7 +792,7 @@ def run_sparse_cycle(args):
 
     # eager: every step builds its context (metadata H2D) and launches from Python
     per_state = {0: [], 1: [], 2: []}
-    cycles = max(1, min(args.steps // 32, 3))
+    cycles = max(1, min(steps // 32, 3))
     for _ in range(blk):  # warm-up cycle, also fills the caches
         step(sparse_seqs)
         advance()
@@ -823,13 +847,13 @@ def run_sparse_cycle(args):
         with torch.cuda.graph(graph_dense, stream=side):
             step(dense_seqs, ctx_d)
     torch.cuda.current_stream().wait_stream(side)
-    graph_dense_ms = timed(lambda: graph_dense.replay(), max(2, min(args.steps, 10)))
+    graph_dense_ms = timed(lambda: graph_dense.replay(), max(2, min(steps, 10)))
     graph_state_ms = {st: timed(lambda: graphs[st].replay(), 3) for st in (0, 1, 2)}
     if ops.read_device_status(dev) != 0:
         raise RuntimeError("a kernel reported a device error")
     sparse_step_ms = statistics.median(cycle_ms) / blk
     line = {
-        "workload": args.workload, "desc": desc, "n_gpus": world,
+        "workload": workload, "desc": desc, "n_gpus": world,
         "parallelism": f"tp{world} head-sharded" if world > 1 else "single GPU",
         "layers": layers, "heads": [Hq_all, Hkv_all], "batch": B, "seq_lens": [min(lens), max(lens)],
         "tokens_dense_step": N_full, "retention_ratio": ratio, "n_keep": [min(n_keeps), max(n_keeps)],
@@ -847,12 +871,11 @@ def run_sparse_cycle(args):
         "note": "attention path only (per layer: selection/store, cache gather, varlen attention); "
                 "timed with CUDA events, max over ranks",
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-        dist.destroy_process_group()
-    return 0
+    for st in graphs.values():
+        del st
+    graphs.clear()
+    del graph_dense
+    return line
 
 
 def run_kernels_case(args):

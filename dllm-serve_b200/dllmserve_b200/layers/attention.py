@@ -65,12 +65,18 @@ class Attention(nn.Module):
         # (device int64); kept only when ``record_selection`` is set.
         self.record_selection = False
         self.last_selection: dict = {}
+        self._cache_sig = None  # (k_cache, v_cache, k_cache ptr, validated paged-cache arguments)
+        self._launch_key = ("attn", num_heads, num_kv_heads, head_dim, scale)
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        context = get_context()
+        if context.is_diffusion and q.dim() in (2, 3) and k.dim() == q.dim() and v.dim() == q.dim():
+            # token-row layouts ([N, heads*D] or [N, heads, D]) go to the
+            # launch as they are (no per-layer views)
+            return self._diffusion_attention(q, k, v, context)
         q = q.view(-1, self.num_heads, self.head_dim)
         k = k.view(-1, self.num_kv_heads, self.head_dim)
         v = v.view(-1, self.num_kv_heads, self.head_dim)
-        context = get_context()
         if context.is_diffusion:
             return self._diffusion_attention(q, k, v, context)
         if self.k_cache.numel() and self.v_cache.numel():
@@ -88,27 +94,42 @@ class Attention(nn.Module):
         return o.view(-1, self.num_heads * self.head_dim)
 
     def _diffusion_attention(self, q, k, v, context):
+        """q [N, num_heads*D] or [N, num_heads, D]; k, v likewise with
+        num_kv_heads; returns [N, num_heads*D]."""
         plan = _plan_for(context, q)
         dev = q.device
+        H, Hk, D = self.num_heads, self.num_kv_heads, self.head_dim
         if self.record_selection:
             self.last_selection = {}
-        for head_select in (True, False):
-            arrs = selection_arrays(plan, head_select, self.num_kv_heads, dev)
-            if arrs is None:
-                continue
-            desc, slots, max_klen, idx_total = arrs
-            top_idx = None
-            if self.record_selection:
-                top_idx = torch.empty(idx_total, dtype=torch.int64, device=dev)
-                self.last_selection[head_select] = top_idx
-            ops.select_kv_store(q, k, v, desc, max_klen, head_select,
-                                self.k_cache, self.v_cache, slots, top_idx)
-        out = torch.empty((q.shape[0], self.num_heads, self.head_dim), dtype=q.dtype, device=dev)
-        if plan.total_c > 0:
-            # reuse state: cached rows read straight from the paged cache
-            ops.varlen_attention(q, k, v, plan.cu, plan.cu, plan.max_rows, self.scale,
-                                 k_cache=self.k_cache, v_cache=self.v_cache, slots=plan.slots_c,
-                                 cu_seqlens_slots=plan.cu_c, out=out)
-        else:
-            ops.varlen_attention(q, k, v, plan.cu, plan.cu, plan.max_rows, self.scale, out=out)
-        return out.view(-1, self.num_heads * self.head_dim)
+        if plan.sel:
+            qv, kv_, vv = q.view(-1, H, D), k.view(-1, Hk, D), v.view(-1, Hk, D)
+            for head_select in (True, False):
+                arrs = selection_arrays(plan, head_select, Hk, dev)
+                if arrs is None:
+                    continue
+                desc, slots, max_klen, idx_total = arrs
+                top_idx = None
+                if self.record_selection:
+                    top_idx = torch.empty(idx_total, dtype=torch.int64, device=dev)
+                    self.last_selection[head_select] = top_idx
+                ops.select_kv_store(qv, kv_, vv, desc, max_klen, head_select,
+                                    self.k_cache, self.v_cache, slots, top_idx)
+        out = torch.empty((q.shape[0], H * D), dtype=q.dtype, device=dev)
+        launch = plan.scratch.get(self._launch_key)
+        if launch is None:
+            # step-level arguments validated once per plan, shared by the layers of this shape
+            launch = ops.prepare_attention(
+                plan.cu, plan.cu, plan.max_rows, plan.total_rows, H, Hk, D, self.scale, dev,
+                slots=plan.slots_c, cu_seqlens_slots=plan.cu_c)
+            plan.scratch[self._launch_key] = launch
+        return launch(q, k, v, out, self._paged_cache_args() if plan.total_c > 0 else None)
+
+    def _paged_cache_args(self):
+        """Validated pointer/size arguments of the bound paged cache, recomputed
+        only when the k_cache / v_cache tensors or their storage change."""
+        kc, vc = self.k_cache, self.v_cache
+        cs = self._cache_sig
+        if cs is None or cs[0] is not kc or cs[1] is not vc or cs[2] != kc.data_ptr():
+            self._cache_sig = cs = (kc, vc, kc.data_ptr(),
+                                    ops.paged_cache_args(kc, vc, self.num_kv_heads, self.head_dim))
+        return cs[3]

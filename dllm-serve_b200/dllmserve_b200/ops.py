@@ -277,6 +277,113 @@ def varlen_attention(
     return out
 
 
+class AttentionLaunch:
+    """A varlen attention launch whose step-level arguments (sequence offsets,
+    maximum query length, head counts, scale and, for reuse steps, the slot
+    list) were validated once; each call checks only what can differ per call
+    (q/k/v/out layout and row counts) and passes a prepared argument tuple to
+    the C ABI, whose own checks (alignment, strides, sizes) still run on every
+    call. One object serves every layer of a step that shares these arguments
+    (layers differ only in their q/k/v and, for reuse steps, their paged
+    cache, given per call as ``paged_cache_args``). Built by
+    ``prepare_attention``."""
+
+    __slots__ = ("_fn", "_slots", "_tail", "_dev", "_dev_index", "_heads", "_rows", "_status", "_ws")
+
+    def __init__(self, fn, slots, tail, dev, heads, rows):
+        self._fn = fn
+        self._slots = slots          # (slots ptr, cu_seqlens_slots ptr) of a paged launch, else None
+        self._tail = tail
+        self._dev = dev
+        self._dev_index = dev.index if dev.index is not None else torch.cuda.current_device()
+        self._heads = heads          # (Hq, Hkv, D)
+        self._rows = rows            # rows of q (and of the fresh k/v)
+        self._status = _status_ptr(dev)
+        self._ws: dict = {}
+
+    def __call__(self, q, k, v, out, cache_args=None):
+        """q/out: [rows, Hq*D] or [rows, Hq, D]; k/v likewise with Hkv (any
+        token stride, heads contiguous). Returns out."""
+        Hq, Hkv, D = self._heads
+        rows, idx = self._rows, self._dev_index
+        for name, t, h in (("q", q, Hq), ("k", k, Hkv), ("v", v, Hkv), ("out", out, Hq)):
+            if t.dtype is not torch.bfloat16 or t.get_device() != idx or t.shape[0] != rows:
+                ok = False
+            elif t.dim() == 2:
+                ok = t.shape[1] == h * D and t.stride(1) == 1
+            else:
+                ok = (t.dim() == 3 and t.shape[1] == h and t.shape[2] == D and t.stride(2) == 1
+                      and t.stride(1) == D)
+            if not ok:
+                raise ValueError(f"{name}: expected bfloat16 [{rows}, {h}*{D}] or [{rows}, {h}, {D}] with "
+                                 f"contiguous heads on {self._dev}, got {t.dtype} {tuple(t.shape)} "
+                                 f"strides {t.stride()}")
+        if self._slots is not None:
+            if cache_args is None or cache_args[2] != Hkv * D:
+                raise ValueError("a paged launch needs paged_cache_args of num_kv_heads * head_dim rows")
+            mid = tuple(cache_args) + self._slots
+        else:
+            mid = ()
+        with _on_device(self._dev):
+            stream = _raw_stream(idx) if _raw_stream is not None else _stream_ptr()
+            ws = self._ws.get(stream)
+            if ws is None:
+                ws = sched_workspace(self._dev, stream)
+                if ws:
+                    self._ws[stream] = ws
+            rc = self._fn(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                          *mid, out.data_ptr(), out.stride(0), *self._tail, ws, self._status, stream)
+        if rc:
+            _native.check(rc, "varlen_attention")
+        LAUNCHES[0] += 1
+        return out
+
+
+def paged_cache_args(k_cache, v_cache, num_kv_heads, head_dim) -> tuple:
+    """(k_cache ptr, v_cache ptr, slot row length, number of slots) of a paged
+    KV cache [blocks, block_size, num_kv_heads, head_dim] (bf16, contiguous)."""
+    if k_cache.device.type != "cuda" or v_cache.device != k_cache.device:
+        raise ValueError("caches must be CUDA tensors on one device")
+    if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise ValueError("caches must be bfloat16")
+    row = num_kv_heads * head_dim
+    if (k_cache.numel() % row or v_cache.numel() != k_cache.numel()
+            or not k_cache.is_contiguous() or not v_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous [blocks, block_size, num_kv_heads, head_dim]")
+    return (k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row)
+
+
+def prepare_attention(cu_seqlens_q, cu_seqlens_k, max_seqlen_q, total_rows, num_heads, num_kv_heads,
+                      head_dim, softmax_scale, device, *, slots=None,
+                      cu_seqlens_slots=None) -> AttentionLaunch:
+    """Validates the step-level arguments of a varlen attention launch once and
+    returns an AttentionLaunch for q/k/v/out of ``total_rows`` rows. With
+    ``slots`` and ``cu_seqlens_slots`` the keys of sequence b are [its cached
+    rows read by slot from the paged cache given per call ; its fresh rows]
+    (dllm_attn_varlen_paged_fwd)."""
+    if head_dim != 128:
+        raise NotImplementedError("head_dim must be 128")
+    for name, c in (("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+        if c.dtype != torch.int32 or not c.is_contiguous() or c.device != device:
+            raise ValueError(f"{name} must be contiguous int32 on {device}")
+    B = cu_seqlens_q.numel() - 1
+    if cu_seqlens_k.numel() != B + 1:
+        raise ValueError("cu_seqlens_q and cu_seqlens_k sizes differ")
+    lib = _native.lib()
+    tail = (cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), B, int(max_seqlen_q), int(total_rows),
+            int(total_rows), num_heads, num_kv_heads, head_dim, float(softmax_scale))
+    if slots is not None:
+        for name, c in (("slots", slots), ("cu_seqlens_slots", cu_seqlens_slots)):
+            if c is None or c.dtype != torch.int32 or not c.is_contiguous() or c.device != device:
+                raise ValueError(f"{name} must be contiguous int32 on {device}")
+        if cu_seqlens_slots.numel() != B + 1:
+            raise ValueError("cu_seqlens_slots must have batch+1 entries")
+        return AttentionLaunch(lib.dllm_attn_varlen_paged_fwd, (slots.data_ptr(), cu_seqlens_slots.data_ptr()),
+                               tail, device, (num_heads, num_kv_heads, head_dim), total_rows)
+    return AttentionLaunch(lib.dllm_attn_varlen_fwd, None, tail, device,
+                           (num_heads, num_kv_heads, head_dim), total_rows)
+
+
 def _check_paged(q, k_cache, v_cache, slots, cu_seqlens_slots, B, Hkv, D) -> int:
     """Validates the paged-cache arguments; returns the cache row length."""
     _require_cuda(q, k_cache, v_cache, slots, cu_seqlens_slots)
