@@ -58,6 +58,88 @@ DLLM_DEVICE float warp_sum(float v) {
   return v;
 }
 
+DLLM_DEVICE uint64_t shfl_xor_u64(uint64_t v, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
+  return ((uint64_t)hi << 32) | lo;
+}
+
+// Descending bitonic sort of sel[0, p2) (p2 a power of two, 32 <= p2 and
+// p2 / E <= kThreads), called by every thread of the CTA. Element i lives in thread t = i / (32E) * 32 + i % 32, register
+// e = (i / 32) % E, so compare-exchange partners at distance j < 32 are lanes
+// of one warp (shuffles), at 32 <= j < 32E registers of one thread, and only
+// j >= 32E goes through shared memory (one synchronised pass each): the
+// network is the same as the plain shared-memory one, with far fewer passes.
+template <int E>
+DLLM_DEVICE void sort_desc_regs(uint64_t* sel, int p2) {
+  const int t = threadIdx.x, lane = t & 31;
+  const bool act = t < p2 / E;  // whole warps (p2 / E is a multiple of 32)
+  const int base = (t >> 5) * 32 * E + lane;
+  uint64_t x[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = act ? sel[base + e * 32] : 0ull;
+  for (int k = 2; k <= p2; k <<= 1) {
+    if (k > 32 * E) {
+      if (act) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) sel[base + e * 32] = x[e];
+      }
+      __syncthreads();
+      for (int j = k >> 1; j >= 32 * E; j >>= 1) {
+        for (int i = t; i < p2; i += kThreads) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const uint64_t a = sel[i], b = sel[ixj];
+            const bool desc = (i & k) == 0;
+            if (desc ? (a < b) : (a > b)) {
+              sel[i] = b;
+              sel[ixj] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+      if (act) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = sel[base + e * 32];
+      }
+    }
+    if (act) {
+      // partners in this thread's registers (j = 32d), d fixed at compile time
+#pragma unroll
+      for (int d = E / 2; d >= 1; d >>= 1) {
+        if (32 * d <= (k >> 1)) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            if ((e & d) == 0) {
+              const bool desc = ((base + e * 32) & k) == 0;
+              const uint64_t a = x[e], b = x[e | d];
+              const bool swap = desc ? (a < b) : (a > b);
+              x[e] = swap ? b : a;
+              x[e | d] = swap ? a : b;
+            }
+          }
+        }
+      }
+      // partners in other lanes of the warp
+      for (int j = min(k >> 1, 16); j > 0; j >>= 1) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const uint64_t y = shfl_xor_u64(x[e], j);
+          const int i = base + e * 32;
+          const bool lower = (i & j) == 0, desc = (i & k) == 0;
+          x[e] = (lower == desc) ? (x[e] > y ? x[e] : y) : (x[e] < y ? x[e] : y);
+        }
+      }
+    }
+  }
+  if (act) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) sel[base + e * 32] = x[e];
+  }
+  __syncthreads();
+}
+
 // Candidate c of a sequence -> token row offset inside the sequence.
 DLLM_DEVICE int cand_token(int c, int blk_start, int blk_len) {
   return c < blk_start ? c : c + blk_len;
@@ -90,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   const int nq = kHeadSelect ? a.group : a.Hq;  // query heads that score this CTA's rows
   float* q_avg = reinterpret_cast<float*>(smem);
   float* scores = q_avg + nq * kD;
-  int p2max = 1;
+  int p2max = 32;
   while (p2max < a.max_klen) p2max <<= 1;
   uint64_t* sel = reinterpret_cast<uint64_t*>(
       smem + (((size_t)nq * kD * 4 + (size_t)a.max_klen * 4 + 15) & ~(size_t)15));
@@ -106,21 +188,45 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   }
 
   // 1) q_avg = mean over the block's query rows (fp32), attention.py:367 / :315.
+  //    Eight interleaved partial sums (row t into partial t mod 8; rows past
+  //    the last multiple of 8 into partial 0) combined as
+  //    ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)), then an fp32 division. With one
+  //    query head per CTA (MHA head_select: 128 elements) four consecutive
+  //    threads share an element, thread j holding partials 2j and 2j+1, and
+  //    the tree is two shuffles; otherwise a thread keeps all eight.
   const int qh0 = kHeadSelect ? h * a.group : 0;
-  for (int e = threadIdx.x; e < nq * kD; e += kThreads) {
-    const int g = e / kD, dd = e % kD;
+  if (nq * kD * 4 == kThreads) {
+    const int e = threadIdx.x >> 2, j = threadIdx.x & 3;
     const __nv_bfloat16* qp =
-        a.q + (int64_t)(tok_start + blk_start) * a.q_tok_stride + (int64_t)(qh0 + g) * kD + dd;
-    // 8 independent partial sums keep 8 loads in flight per thread
-    float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        a.q + (int64_t)(tok_start + blk_start) * a.q_tok_stride + (int64_t)qh0 * kD + e;
+    float sa = 0.f, sb = 0.f;
     int t = 0;
     for (; t + 8 <= blk_len; t += 8) {
-#pragma unroll
-      for (int u = 0; u < 8; ++u) s8[u] += __bfloat162float(qp[(int64_t)(t + u) * a.q_tok_stride]);
+      sa += __bfloat162float(qp[(int64_t)(t + 2 * j) * a.q_tok_stride]);
+      sb += __bfloat162float(qp[(int64_t)(t + 2 * j + 1) * a.q_tok_stride]);
     }
-    for (; t < blk_len; ++t) s8[0] += __bfloat162float(qp[(int64_t)t * a.q_tok_stride]);
-    const float s = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
-    q_avg[e] = s / (float)blk_len;
+    if (j == 0)
+      for (; t < blk_len; ++t) sa += __bfloat162float(qp[(int64_t)t * a.q_tok_stride]);
+    float p = sa + sb;
+    p += __shfl_xor_sync(0xffffffffu, p, 1);
+    p += __shfl_xor_sync(0xffffffffu, p, 2);
+    if (j == 0) q_avg[e] = p / (float)blk_len;
+  } else {
+    for (int e = threadIdx.x; e < nq * kD; e += kThreads) {
+      const int g = e / kD, dd = e % kD;
+      const __nv_bfloat16* qp =
+          a.q + (int64_t)(tok_start + blk_start) * a.q_tok_stride + (int64_t)(qh0 + g) * kD + dd;
+      // 8 independent partial sums keep 8 loads in flight per thread
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      int t = 0;
+      for (; t + 8 <= blk_len; t += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s8[u] += __bfloat162float(qp[(int64_t)(t + u) * a.q_tok_stride]);
+      }
+      for (; t < blk_len; ++t) s8[0] += __bfloat162float(qp[(int64_t)t * a.q_tok_stride]);
+      const float s = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      q_avg[e] = s / (float)blk_len;
+    }
   }
   if (threadIdx.x == 0) misc[2] = 0;  // selection counter
   if (kHeadSelect) {
@@ -317,26 +423,36 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     }
   }
   const int n_sel = full_sort ? Klen : n_keep;
-  int p2 = 1;
+  int p2 = 32;
   while (p2 < n_sel) p2 <<= 1;
   for (int i = n_sel + threadIdx.x; i < p2; i += kThreads) sel[i] = 0;  // padding sorts last
   __syncthreads();
 
-  // 6) descending bitonic sort of the n_keep selected keys, attention.py:402-404 / :341.
-  for (int k = 2; k <= p2; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < p2; i += kThreads) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t x = sel[i], y = sel[ixj];
-          const bool desc = (i & k) == 0;
-          if (desc ? (x < y) : (x > y)) {
-            sel[i] = y;
-            sel[ixj] = x;
+  // 6) descending sort of the n_sel selected keys, attention.py:402-404 / :341.
+  if (p2 <= kThreads) {
+    sort_desc_regs<1>(sel, p2);
+  } else if (p2 <= 2 * kThreads) {
+    sort_desc_regs<2>(sel, p2);
+  } else if (p2 <= 4 * kThreads) {
+    sort_desc_regs<4>(sel, p2);
+  } else if (p2 <= 8 * kThreads) {
+    sort_desc_regs<8>(sel, p2);
+  } else {
+    for (int k = 2; k <= p2; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < p2; i += kThreads) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const uint64_t x = sel[i], y = sel[ixj];
+            const bool desc = (i & k) == 0;
+            if (desc ? (x < y) : (x > y)) {
+              sel[i] = y;
+              sel[ixj] = x;
+            }
           }
         }
+        __syncthreads();
       }
-      __syncthreads();
     }
   }
 
@@ -409,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
 }  // namespace
 
 size_t select_kv_smem_bytes(int nq, int max_klen) {
-  int p2 = 1;
+  int p2 = 32;
   while (p2 < max_klen) p2 <<= 1;
   const size_t head = (((size_t)nq * kD * 4 + (size_t)max_klen * 4 + 15) & ~(size_t)15);
   return head + (size_t)p2 * 8 + (256 + kWarps + 4) * 4;
