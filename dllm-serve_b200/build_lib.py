@@ -19,7 +19,8 @@ REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 OUT = os.path.join(HERE, "dllmserve_b200", "libdllm_attn.so")
-SOURCES = ["attn_fwd.cu", "attn_fwd_split.cu", "kvcache.cu", "select_kv.cu", "rope.cu", "capi.cu"]
+SOURCES = ["attn_fwd.cu", "attn_fwd_split.cu", "kvcache.cu", "select_kv.cu", "rope.cu", "step_plan.cu",
+           "capi.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -12,6 +12,7 @@
 #include "kvcache.h"
 #include "select_kv.h"
 #include "rope.h"
+#include "step_plan.h"
 
 namespace {
 
@@ -481,6 +482,52 @@ int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const void* k, int
   cudaError_t e = dllm::launch_select_kv(a, head_select != 0, n_seqs,
                                          reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "select_kv launch");
+  return DLLM_OK;
+}
+
+int dllm_build_step_plan(const int64_t* seqs, int batch, int num_kv_heads, int32_t* out,
+                         const int64_t* layout, int32_t* err_flag, void* stream) {
+  static_assert(DLLM_PLAN_SEQ_FIELDS == dllm::kPlanSeqFields, "plan row layout");
+  static_assert(DLLM_SEQ_DESC_INTS == dllm::kPlanDescInts, "descriptor layout");
+  if (batch < 0 || num_kv_heads <= 0) return fail(DLLM_ERR_INVALID_ARG, "negative batch or num_kv_heads <= 0");
+  if (batch > dllm::step_plan_max_batch() || batch > DLLM_PLAN_MAX_BATCH)
+    return fail(DLLM_ERR_TOO_LARGE, "batch %d > %d", batch, DLLM_PLAN_MAX_BATCH);
+  if (batch == 0) return DLLM_OK;
+  if (seqs == nullptr || out == nullptr || layout == nullptr) return fail(DLLM_ERR_INVALID_ARG, "null pointer");
+  if (!aligned(seqs, 8) || !aligned(out, 4)) return fail(DLLM_ERR_ALIGNMENT, "seqs / out misaligned");
+  // sections in order, inside the buffer: cu | cu_c | desc_hs | desc_sh | slots_c | slots_hs | slots_sh
+  const int64_t total = layout[0];
+  const int64_t sec[6][2] = {{layout[1], batch + 1},
+                             {layout[2], layout[3] * DLLM_SEQ_DESC_INTS},
+                             {layout[4], layout[5] * DLLM_SEQ_DESC_INTS},
+                             {layout[6], layout[7]},
+                             {layout[8], layout[9]},
+                             {layout[10], layout[11]}};
+  int64_t end = batch + 1;
+  for (int i = 0; i < 6; ++i) {
+    if (sec[i][1] < 0 || sec[i][0] < end) return fail(DLLM_ERR_INVALID_ARG, "plan layout section %d overlaps", i);
+    end = sec[i][0] + sec[i][1];
+  }
+  if (end > total || total >= ((int64_t)1 << 31)) return fail(DLLM_ERR_INVALID_ARG, "plan layout exceeds the buffer");
+  dllm::StepPlanArgs a;
+  a.seqs = seqs;
+  a.batch = batch;
+  a.num_kv_heads = num_kv_heads;
+  a.out = out;
+  a.off_cu_c = (int)layout[1];
+  a.off_desc_hs = (int)layout[2];
+  a.cap_desc_hs = (int)layout[3];
+  a.off_desc_sh = (int)layout[4];
+  a.cap_desc_sh = (int)layout[5];
+  a.off_slots_c = (int)layout[6];
+  a.cap_slots_c = (int)layout[7];
+  a.off_slots_hs = (int)layout[8];
+  a.cap_slots_hs = (int)layout[9];
+  a.off_slots_sh = (int)layout[10];
+  a.cap_slots_sh = (int)layout[11];
+  a.err = err_flag;
+  cudaError_t e = dllm::launch_step_plan(a, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "step plan launch");
   return DLLM_OK;
 }
 

@@ -23,6 +23,9 @@ DLLM_DEV_WAIT_TIMEOUT = 2
 DLLM_DEV_BAD_SEQUENCE = 3
 
 SEQ_DESC_INTS = 8
+PLAN_SEQ_FIELDS = 10   # DLLM_PLAN_SEQ_FIELDS
+PLAN_LAYOUT_INTS = 12  # DLLM_PLAN_LAYOUT_INTS
+PLAN_MAX_BATCH = 1024  # DLLM_PLAN_MAX_BATCH
 SCHED_WORKSPACE_INTS = 2  # DLLM_SCHED_WORKSPACE_INTS
 
 # Every exported entry point with its (argtypes, restype).
@@ -62,6 +65,7 @@ SIGNATURES = {
         [_P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _I, _I, _P, _P],
         _I,
     ),
+    "dllm_build_step_plan": ([_P, _I, _I, _P, _P, _P, _P], _I),
     "dllm_select_kv_store": (
         [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _I64, _P, _P, _P, _P],
         _I,

@@ -25,9 +25,13 @@ Per-sequence rules (same as the reference):
 """
 from __future__ import annotations
 
+import ctypes
+import struct
 from dataclasses import dataclass, field
 
 import torch
+
+from .. import _native, ops
 
 from ..sparse.state import num_keep
 
@@ -88,16 +92,14 @@ def _h2d(values, device, dtype=torch.int32) -> torch.Tensor:
     return t
 
 
-def build_step_plan(ctx, device: torch.device, total_rows: int) -> StepPlan:
-    """Turn the context of one diffusion step into device metadata.
-
-    ``total_rows`` is q.shape[0]; the per-sequence row counts derived from the
-    sparse states must add up to it (the model runner's layout)."""
+def _seq_infos(ctx, total_rows: int):
+    """Per-sequence rows, block, cached / selected row counts (the reference's
+    per-sequence rules, attention.py:168-304) and the validated slot lists."""
     seqs = ctx.seqs
     if not seqs:
         raise ValueError("diffusion context without sequences")
     slot_mapping = ctx.slot_mapping
-    infos = []
+    infos, slot_lists = [], []
     row = 0
     for i, seq in enumerate(seqs):
         st = seq_state(seq)
@@ -121,17 +123,132 @@ def build_step_plan(ctx, device: torch.device, total_rows: int) -> StepPlan:
                            head_select=bool(ss.config.head_select))
         else:
             info = SeqInfo(STATE_DENSE, L, row)
+        sm = None
         if st != STATE_DENSE:
             n_expect = info.n_cached if st == STATE_REUSE else info.n_keep
             sm = slot_mapping[i] if slot_mapping is not None else None
-            if sm is None or sm.numel() != n_expect:
-                got = None if sm is None else sm.numel()
+            if sm is None or not isinstance(sm, torch.Tensor) or sm.numel() != n_expect:
+                got = None if not isinstance(sm, torch.Tensor) else sm.numel()
                 raise ValueError(
                     f"slot_mapping[{i}] has {got} slots, sequence needs {n_expect}")
         infos.append(info)
+        slot_lists.append(sm)
         row += info.rows
     if row != total_rows:
         raise ValueError(f"sequences cover {row} rows but q has {total_rows}")
+    return infos, slot_lists
+
+
+class _Staging:
+    """A ring of pinned host buffers for the per-sequence rows of the device
+    plan builder; a buffer is reused only after the copy that read it ran."""
+
+    def __init__(self, n=4):
+        self.bufs = [None] * n
+        self.events = [None] * n
+        self.next = 0
+
+    def take(self, rows: int, device):
+        i = self.next
+        self.next = (i + 1) % len(self.bufs)
+        ev = self.events[i]
+        if ev is not None:
+            ev.synchronize()
+        if self.bufs[i] is None:
+            self.bufs[i] = torch.empty((_native.PLAN_MAX_BATCH, _native.PLAN_SEQ_FIELDS),
+                                       dtype=torch.int64, pin_memory=True)
+        return i, self.bufs[i]
+
+    def done(self, i):
+        ev = torch.cuda.Event()
+        ev.record()
+        self.events[i] = ev
+
+
+_STAGING: dict = {}
+
+
+def _device_plan(ctx, device, total_rows, num_kv_heads, infos, slot_lists) -> "StepPlan":
+    """Materialise the plan with one dllm_build_step_plan launch: the device
+    re-derives every per-sequence quantity from the sequences' raw state and
+    writes cu, cu_c, the selection descriptors and the concatenated slot
+    lists into one int32 buffer whose sections become the plan's tensors."""
+    B = len(infos)
+    n_hs = sum(1 for f in infos if f.state == STATE_COMPUTE and f.head_select)
+    n_sh = sum(1 for f in infos if f.state == STATE_COMPUTE and not f.head_select)
+    total_c = sum(f.n_cached for f in infos if f.state == STATE_REUSE)
+    slots_hs = sum(f.n_keep for f in infos if f.state == STATE_COMPUTE and f.head_select)
+    slots_sh = sum(f.n_keep for f in infos if f.state == STATE_COMPUTE and not f.head_select)
+    D8 = _native.SEQ_DESC_INTS
+    off_cu_c = B + 1
+    off_dhs = off_cu_c + B + 1
+    off_dsh = off_dhs + n_hs * D8
+    off_sc = off_dsh + n_sh * D8
+    off_shs = off_sc + total_c
+    off_ssh = off_shs + slots_hs
+    total = off_ssh + slots_sh
+    layout = (ctypes.c_int64 * _native.PLAN_LAYOUT_INTS)(
+        total, off_cu_c, off_dhs, n_hs, off_dsh, n_sh, off_sc, total_c, off_shs, slots_hs, off_ssh, slots_sh)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    staging = _STAGING.get(idx)
+    if staging is None:
+        staging = _STAGING[idx] = _Staging()
+    keep = []
+    si, buf = staging.take(B, device)
+    rows = []
+    for f, seq, sm in zip(infos, ctx.seqs, slot_lists):
+        ss = getattr(seq, "sparse_state", None)
+        if f.state == STATE_DENSE:
+            rows.append([0, int(seq.num_tokens), int(seq.num_prompt_tokens), 0, 0, 0, 0, 0, 0, 0])
+            continue
+        if sm.dtype != torch.int32 or not sm.is_contiguous() or sm.device != device:
+            sm = sm.to(device=device, dtype=torch.int32).contiguous()
+            keep.append(sm)
+        pool = ss.pool_kernel if ss.pool_kernel is not None else 1
+        ratio_bits = struct.unpack("<q", struct.pack("<d", float(ss.retention_ratio)))[0]
+        rows.append([f.state, int(seq.num_tokens), int(seq.num_prompt_tokens), int(ss.current_block_idx),
+                     int(ss.block_len), ratio_bits, int(pool) | (int(bool(ss.config.head_select)) << 32),
+                     sm.data_ptr(), sm.numel(), 0])
+    buf[:B] = torch.tensor(rows, dtype=torch.int64)
+    with torch.cuda.device(device):
+        dev_rows = torch.empty((B, _native.PLAN_SEQ_FIELDS), dtype=torch.int64, device=device)
+        dev_rows.copy_(buf[:B], non_blocking=True)
+        staging.done(si)
+        out = torch.empty(total, dtype=torch.int32, device=device)
+        rc = _native.lib().dllm_build_step_plan(dev_rows.data_ptr(), B, int(num_kv_heads), out.data_ptr(),
+                                                layout, ops._status_ptr(device), ops._stream_ptr())
+    _native.check(rc, "build_step_plan")
+    ops.LAUNCHES[0] += 1
+    keep += [dev_rows, out] + [sm for sm in slot_lists if sm is not None]
+    plan = StepPlan(infos=infos, cu=out[:B + 1], max_rows=max(f.rows for f in infos), total_rows=total_rows,
+                    cu_c=out[off_cu_c:off_cu_c + B + 1] if total_c else None,
+                    slots_c=out[off_sc:off_sc + total_c] if total_c else None, total_c=total_c)
+    for hs, n, off_d, off_s, n_slots in ((True, n_hs, off_dhs, off_shs, slots_hs),
+                                         (False, n_sh, off_dsh, off_ssh, slots_sh)):
+        if not n:
+            continue
+        sel_idx = [i for i, f in enumerate(infos) if f.state == STATE_COMPUTE and f.head_select == hs]
+        max_klen = max(infos[i].rows - infos[i].blk_len for i in sel_idx)
+        mult = num_kv_heads if hs else 1
+        plan.sel[hs] = (sel_idx, None, out[off_s:off_s + n_slots], max_klen)
+        plan.scratch[("sel", hs, num_kv_heads)] = (out[off_d:off_d + n * D8].view(n, D8),
+                                                    out[off_s:off_s + n_slots], max_klen, n_slots * mult)
+    plan.scratch["keepalive"] = keep
+    return plan
+
+
+def build_step_plan(ctx, device: torch.device, total_rows: int, num_kv_heads: int | None = None) -> StepPlan:
+    """Turn the context of one diffusion step into device metadata.
+
+    ``total_rows`` is q.shape[0]; the per-sequence row counts derived from the
+    sparse states must add up to it (the model runner's layout). On a CUDA
+    device with ``num_kv_heads`` given, the arrays are built by one device
+    launch (dllm_build_step_plan); otherwise (CPU, used by host-logic tests)
+    they are assembled here."""
+    infos, slot_lists = _seq_infos(ctx, total_rows)
+    if (device.type == "cuda" and num_kv_heads is not None and len(infos) <= _native.PLAN_MAX_BATCH):
+        return _device_plan(ctx, device, total_rows, num_kv_heads, infos, slot_lists)
+    slot_mapping = ctx.slot_mapping
 
     cu_host = [0]
     for inf in infos:
@@ -188,6 +305,9 @@ def selection_arrays(plan: StepPlan, head_select: bool, num_kv_heads: int, devic
     if cached is not None:
         return cached
     idx, desc, slots, max_klen = entry
+    if desc is None:
+        raise ValueError("this step plan was built on the device for another num_kv_heads; "
+                         "build one per num_kv_heads")
     rows = []
     idx_off = 0
     for d in desc:

@@ -35,7 +35,7 @@ load_kvcache = ops.load_kvcache
 _PLAN_ATTR = "_dllm_b200_plans"
 
 
-def _plan_for(ctx, q: torch.Tensor):
+def _plan_for(ctx, q: torch.Tensor, num_kv_heads: int):
     plans = getattr(ctx, _PLAN_ATTR, None)
     if plans is None:
         plans = {}
@@ -43,10 +43,10 @@ def _plan_for(ctx, q: torch.Tensor):
             setattr(ctx, _PLAN_ATTR, plans)
         except AttributeError:  # a frozen context: rebuild per layer
             pass
-    key = (q.device, q.shape[0])
+    key = (q.device, q.shape[0], num_kv_heads)
     plan = plans.get(key)
     if plan is None:
-        plan = build_step_plan(ctx, q.device, q.shape[0])
+        plan = build_step_plan(ctx, q.device, q.shape[0], num_kv_heads)
         plans[key] = plan
     return plan
 
@@ -96,7 +96,7 @@ class Attention(nn.Module):
     def _diffusion_attention(self, q, k, v, context):
         """q [N, num_heads*D] or [N, num_heads, D]; k, v likewise with
         num_kv_heads; returns [N, num_heads*D]."""
-        plan = _plan_for(context, q)
+        plan = _plan_for(context, q, self.num_kv_heads)
         dev = q.device
         H, Hk, D = self.num_heads, self.num_kv_heads, self.head_dim
         if self.record_selection:

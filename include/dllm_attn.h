@@ -25,6 +25,8 @@
  *   dllm_rope_neox            <- RotaryEmbedding.forward / apply_rotary_emb
  *                                (dllmserve/layers/rotary_embedding.py:6-16, 41-57), the
  *                                op the decoder layers apply to q, k just before attention
+ *   dllm_build_step_plan      <- the per-sequence metadata of attention.py:168-304 /
+ *                                model_runner.py:240-321, on the device
  *   dllm_select_kv_store      <- _select_important_head_kv (attention.py:344-413) or
  *                                _select_important_kv (attention.py:308-342), followed by
  *                                the k_prefix_suffix[idx] gather and store_kvcache of the
@@ -285,6 +287,40 @@ DLLM_API int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const voi
                          int head_select, void* k_cache, void* v_cache, int64_t cache_tok_stride,
                          int64_t num_slots, const int32_t* slots, int64_t* top_idx,
                          int32_t* err_flag, void* stream);
+
+/*
+ * Per-step metadata of the diffusion attention path, built on the device in one
+ * launch. Replaces the per-sequence host loop that the reference runs inside every
+ * layer (attention.py:168-304: which rows a sequence contributes, its block, the
+ * cached rows it attends or the rows it selects) with the sizing rules of
+ * sparse/state.py:44-62 (block boundaries) and engine/sequence.py:98-152 (n_keep),
+ * and the packing of ModelRunner._run_diffusion (model_runner.py:240-321).
+ * seqs: device int64 [batch, DLLM_PLAN_SEQ_FIELDS], per sequence in batch order:
+ *   [0] cache state: 0 dense, 1 compute cache, 2 reuse cache
+ *   [1] num_tokens L    [2] num_prompt_tokens P    [3] current block index
+ *   [4] block length (SparseConfig.default_block_len)
+ *   [5] retention ratio as the bits of an IEEE float64
+ *   [6] pool_kernel | head_select << 32
+ *   [7] device pointer of the sequence's slot list (int32), 0 for a dense sequence
+ *   [8] its number of slots (must equal n_keep: min(max(1, int(Klen*r)), Klen))
+ *   [9] 0
+ * out: device int32 buffer; layout: HOST int64[DLLM_PLAN_LAYOUT_INTS] = {total ints,
+ *   offset of cu_c, offset and capacity (rows) of the head_select descriptors, of the
+ *   shared-ranking descriptors, offset and capacity of the reuse slots, of the
+ *   head_select slots, of the shared-ranking slots}. cu (batch+1 row offsets) is at 0.
+ * Written: cu [batch+1], cu_c [batch+1] (cached rows of reuse sequences), one
+ * DLLM_SEQ_DESC_INTS descriptor per compute-cache sequence of each head_select flavour
+ * (batch order; idx_off for a top_idx laid out [num_kv_heads, n_keep] per sequence with
+ * head_select), and the concatenated slot lists of the reuse sequences and of each
+ * selection flavour. A slot count that differs from the rule, an empty block in the
+ * compute-cache state or an overflowing section sets DLLM_DEV_BAD_SEQUENCE in err_flag.
+ * batch <= DLLM_PLAN_MAX_BATCH.
+ */
+#define DLLM_PLAN_SEQ_FIELDS 10
+#define DLLM_PLAN_LAYOUT_INTS 12
+#define DLLM_PLAN_MAX_BATCH 1024
+DLLM_API int dllm_build_step_plan(const int64_t* seqs, int batch, int num_kv_heads, int32_t* out,
+                                  const int64_t* layout, int32_t* err_flag, void* stream);
 
 #ifdef __cplusplus
 }
