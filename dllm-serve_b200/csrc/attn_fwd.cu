@@ -128,16 +128,19 @@ struct Unit {
 // a sequence and head (their K/V stay hot in L2 while several CTAs read them).
 DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
   Unit r;
-  const int per_b = a.Hq * a.qunits;
+  const int per_b = a.n_heads * a.qunits;
   const int b = u / per_b;
   const int rem = u - b * per_b;
-  r.hq = rem / a.qunits;
-  const int p = rem - r.hq * a.qunits;
+  const int hsel = rem / a.qunits;
+  const int p = rem - hsel * a.qunits;
+  r.hq = a.head_idx != nullptr ? a.head_idx[hsel] : hsel;
+  const bool head_ok = r.hq >= 0 && r.hq < a.Hq;
+  if (!head_ok) r.hq = 0;
   r.hkv = r.hq / a.group;
   r.q_begin = a.cu_q[b];
   r.Lq = a.cu_q[b + 1] - r.q_begin;
   r.q0 = p * 2 * kTileM;
-  r.valid = r.q0 < r.Lq;
+  r.valid = head_ok && r.q0 < r.Lq;
   r.ntiles = (r.Lq - r.q0 > kTileM) ? 2 : 1;
   r.k_begin = a.cu_k[b];
   r.nk = a.cu_k[b + 1] - r.k_begin;
@@ -277,7 +280,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             return r;
           };
           u = n == 0 ? (int)blockIdx.x : claim();
-          while (u < total_units && !decode_unit(u, args).valid) u = claim();
+          while (u < total_units && !decode_unit(u, args).valid) {
+            if (args.head_idx != nullptr) {
+              const int hs = (u % (args.n_heads * args.qunits)) / args.qunits;
+              const int hq = args.head_idx[hs];
+              if (hq < 0 || hq >= args.Hq) set_error(args.err, kDevBadSequence);
+            }
+            u = claim();
+          }
           uring[n % kRing] = u < total_units ? u : -2;
           mbar_arrive(bar(BAR_UFULL + n % kRing));
         }
@@ -653,7 +663,8 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, cons
   }
   AttnKernelArgs a = args;
   a.qunits = (max_q + 2 * kTileM - 1) / (2 * kTileM);
-  const long long units = (long long)a.B * a.Hq * a.qunits;
+  if (a.head_idx == nullptr) a.n_heads = a.Hq;
+  const long long units = (long long)a.B * a.n_heads * a.qunits;
   if (units == 0) return cudaSuccess;
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_units = (int)units;

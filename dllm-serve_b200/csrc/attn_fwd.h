@@ -37,9 +37,15 @@ struct AttnKernelArgs {
   // segment <= 128 / qpack rows; the Q tensor map's box is then (64, qpack,
   // 128 / qpack)). 1: one head per tile. The pair kernel requires 1.
   int qpack;
+  // Query heads of the launch: head_idx[0 .. n_heads) when head_idx is set
+  // (units are numbered over that list, so heads left out cost nothing; an
+  // index outside [0, Hq) flags kDevBadSequence and its units are skipped),
+  // else all Hq heads (n_heads = Hq). Requires qpack == 1.
+  const int32_t* head_idx;
+  int n_heads;
   int qunits;              // query units per (sequence, head): 256-row tile pairs (pair
                            // kernel) or 128-row tiles (split kernel); set by the launcher
-  int total_units;         // B * Hq * qunits; set by the launcher
+  int total_units;         // B * n_heads * qunits; set by the launcher
   // Rotary embedding applied on chip (split kernel only; null positions: off).
   // Query row r and fresh key row r are rotated by cos_sin[positions[r]]
   // between their TMA arrival and the MMA that reads them; cached rows are

@@ -155,6 +155,7 @@ struct Unit {
 DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
   Unit r;
   int b, t;
+  bool head_ok = true;
   if (a.qpack > 1) {
     const int per_b = a.Hkv * a.qunits;
     b = u / per_b;
@@ -165,18 +166,24 @@ DLLM_DEVICE Unit decode_unit(int u, const AttnKernelArgs& a) {
     r.nheads = min(a.qpack, a.group - c * a.qpack);
     t = 0;
   } else {
-    const int per_b = a.Hq * a.qunits;
+    const int per_b = a.n_heads * a.qunits;
     b = u / per_b;
     const int rem = u - b * per_b;
-    r.hq = rem / a.qunits;
-    t = rem - r.hq * a.qunits;
+    const int hsel = rem / a.qunits;
+    t = rem - hsel * a.qunits;
+    r.hq = a.head_idx != nullptr ? a.head_idx[hsel] : hsel;
+    head_ok = r.hq >= 0 && r.hq < a.Hq;
+    if (!head_ok) {
+      set_error(a.err, kDevBadSequence);
+      r.hq = 0;
+    }
     r.hkv = r.hq / a.group;
     r.nheads = 1;
   }
   r.q_begin = a.cu_q[b];
   r.Lq = a.cu_q[b + 1] - r.q_begin;
   r.q0 = t * kTileM;
-  r.valid = r.q0 < r.Lq;
+  r.valid = head_ok && r.q0 < r.Lq;
   r.k_begin = a.cu_k[b];
   r.nk = a.cu_k[b + 1] - r.k_begin;
   r.c_begin = 0;
@@ -833,7 +840,8 @@ cudaError_t launch_attn_fwd_split(const CUtensorMap& tmQ, const CUtensorMap& tmK
     units = (long long)a.B * a.Hkv * a.qunits;
   } else {
     a.qunits = (max_q + split::kTileM - 1) / split::kTileM;
-    units = (long long)a.B * a.Hq * a.qunits;
+    if (a.head_idx == nullptr) a.n_heads = a.Hq;
+    units = (long long)a.B * a.n_heads * a.qunits;
   }
   if (units == 0) return cudaSuccess;
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;

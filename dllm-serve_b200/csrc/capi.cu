@@ -113,7 +113,8 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
                 int max_q, int64_t total_q, int64_t total_k, int64_t total_c, int Hq, int Hkv,
                 int head_dim, float scale, int32_t* sched, int32_t* err, void* stream,
                 const int32_t* slots = nullptr, const int64_t* positions = nullptr,
-                const float* cos_sin = nullptr, int64_t max_position = 0) {
+                const float* cos_sin = nullptr, int64_t max_position = 0,
+                const int32_t* head_idx = nullptr, int n_heads = -1) {
   if (head_dim != 128)
     return fail(DLLM_ERR_UNSUPPORTED, "head_dim %d not supported (only 128)", head_dim);
   if (Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
@@ -134,6 +135,13 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
     if (total_q != total_k)
       return fail(DLLM_ERR_INVALID_ARG, "on-chip rotary needs total_q == total_k (one position per row)");
   }
+  if (head_idx != nullptr) {
+    if (n_heads < 0 || n_heads > Hq)
+      return fail(DLLM_ERR_INVALID_ARG, "num_selected_heads %d outside [0, %d]", n_heads, Hq);
+    if (!aligned(head_idx, 4)) return fail(DLLM_ERR_ALIGNMENT, "head_idx is not 4-byte aligned");
+    if (positions != nullptr) return fail(DLLM_ERR_UNSUPPORTED, "a head list with on-chip rotary");
+    if (n_heads == 0) return DLLM_OK;
+  }
   if (batch == 0 || total_q == 0 || max_q == 0) return DLLM_OK;
   if (cu_q == nullptr || cu_k == nullptr) return fail(DLLM_ERR_INVALID_ARG, "cu_seqlens is null");
   int rc;
@@ -152,7 +160,7 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   // GQA launches whose query segments are short (the reuse steps' blocks) pack
   // m query heads of a KV group into one 128-row tile of the split kernel.
   int qpack = 1;
-  if (max_q <= dllm::kSplitMaxQ) {
+  if (max_q <= dllm::kSplitMaxQ && head_idx == nullptr) {
     for (int m = 4; m >= 2; m >>= 1) {
       if (Hq / Hkv >= m && max_q <= 128 / m) {
         qpack = m;
@@ -196,6 +204,8 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.positions = positions;
   a.cos_sin = cos_sin;
   a.max_position = max_position;
+  a.head_idx = head_idx;
+  a.n_heads = head_idx != nullptr ? n_heads : Hq;
   // Query segments that fit one tile (the reuse steps' fresh blocks) go to the
   // split kernel, which keeps both softmax warpgroups busy on a lone tile.
   const int sms = num_sms_of_current_device();
@@ -390,6 +400,28 @@ int dllm_attn_varlen_rope_fwd(const int64_t* positions, const float* cos_sin_cac
                      slots != nullptr ? num_slots : 0, num_heads, num_kv_heads, head_dim,
                      softmax_scale, nullptr, err_flag, stream, slots, positions, cos_sin_cache,
                      max_position);
+}
+
+int dllm_attn_varlen_heads_fwd(const void* q, int64_t q_tok_stride, const void* k, int64_t k_tok_stride,
+                               const void* v, int64_t v_tok_stride, const void* k_cache,
+                               const void* v_cache, int64_t cache_tok_stride, int64_t num_slots,
+                               const int32_t* slots, const int32_t* cu_seqlens_slots, void* o,
+                               int64_t o_tok_stride, const int32_t* cu_seqlens_q,
+                               const int32_t* cu_seqlens_k, int batch, int max_seqlen_q, int64_t total_q,
+                               int64_t total_k, int num_heads, int num_kv_heads, int head_dim,
+                               float softmax_scale, const int32_t* head_idx, int num_selected_heads,
+                               int32_t* sched_workspace, int32_t* err_flag, void* stream) {
+  if (head_idx == nullptr && num_selected_heads > 0) return fail(DLLM_ERR_INVALID_ARG, "head_idx is null");
+  if ((slots == nullptr) != (cu_seqlens_slots == nullptr))
+    return fail(DLLM_ERR_INVALID_ARG, "slots and cu_seqlens_slots must both be given or both be null");
+  if (slots != nullptr && num_slots <= 0) return fail(DLLM_ERR_INVALID_ARG, "num_slots must be > 0");
+  if (num_selected_heads == 0) return DLLM_OK;
+  return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, k_cache, cache_tok_stride,
+                     v_cache, cache_tok_stride, o, o_tok_stride, cu_seqlens_q, cu_seqlens_k,
+                     cu_seqlens_slots, batch, max_seqlen_q, total_q, total_k,
+                     slots != nullptr ? num_slots : 0, num_heads, num_kv_heads, head_dim,
+                     softmax_scale, sched_workspace, err_flag, stream, slots, nullptr, nullptr, 0,
+                     head_idx, num_selected_heads);
 }
 
 int dllm_rope_neox(const int64_t* positions, const void* q_in, int64_t q_in_stride, void* q_out,

@@ -61,6 +61,11 @@ SIGNATURES = {
          _I, _I, _I64, _I64, _I, _I, _I, _F, _P, _P],
         _I,
     ),
+    "dllm_attn_varlen_heads_fwd": (
+        [_P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _I, _I, _I64, _I64,
+         _I, _I, _I, _F, _P, _I, _P, _P, _P],
+        _I,
+    ),
     "dllm_rope_neox": (
         [_P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _I, _I, _P, _P],
         _I,

@@ -193,6 +193,7 @@ def varlen_attention(
     cu_seqlens_slots: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
     rope: tuple[torch.Tensor, torch.Tensor] | None = None,
+    heads: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Non-causal varlen attention (bf16). With ``k_cached``/``v_cached``/
     ``cu_seqlens_c`` each sequence attends to [cached rows ; fresh rows]; with
@@ -203,7 +204,11 @@ def varlen_attention(
     rotated; the result equals ``rope_neox(positions, q, k, cos_sin_cache)``
     followed by this attention, bit for bit. Launches whose query segments fit
     one 128-row tile rotate on chip (``dllm_attn_varlen_rope_fwd``: q and k are
-    left untouched); longer ones rotate into new tensors first."""
+    left untouched); longer ones rotate into new tensors first.
+
+    ``heads`` (int32 device tensor of query-head indices): only those heads are
+    computed (``dllm_attn_varlen_heads_fwd``); the output rows of the other
+    heads are left as they are (pass ``out`` to keep them meaningful)."""
     if rope is not None:
         positions, cos_sin = rope
         if k_cached is not None:
@@ -237,6 +242,28 @@ def varlen_attention(
             raise ValueError("out must have as many rows as q")
     lib = _native.lib()
     status = _status_ptr(dev)
+    if heads is not None:
+        if heads.dtype != torch.int32 or heads.dim() != 1 or not heads.is_contiguous() or heads.device != dev:
+            raise ValueError("heads must be a contiguous 1-D int32 tensor on the inputs' device")
+        if k_cached is not None or rope is not None:
+            raise ValueError("heads works with the fresh rows or the paged cache (k_cache/slots) only")
+        if k_cache is not None:
+            row = _check_paged(q, k_cache, v_cache, slots, cu_seqlens_slots, B, Hkv, D)
+            cache_args = (k_cache.data_ptr(), v_cache.data_ptr(), row, k_cache.numel() // row,
+                          slots.data_ptr(), cu_seqlens_slots.data_ptr())
+        else:
+            cache_args = (None, None, 0, 0, None, None)
+        with _on_device(dev):
+            stream = _stream_ptr()
+            rc = lib.dllm_attn_varlen_heads_fwd(
+                q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), *cache_args,
+                out.data_ptr(), out.stride(0), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), B,
+                int(max_seqlen_q), q.shape[0], k.shape[0], Hq, Hkv, D, float(softmax_scale),
+                heads.data_ptr(), heads.numel(), sched_workspace(dev, stream), status, stream)
+        _native.check(rc, "varlen_attention(heads)")
+        if B > 0 and q.shape[0] > 0 and heads.numel() > 0:
+            LAUNCHES[0] += 1
+        return out
     with _on_device(dev):
         stream = _stream_ptr()
         sched = sched_workspace(dev, stream)

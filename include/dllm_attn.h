@@ -25,6 +25,8 @@
  *   dllm_rope_neox            <- RotaryEmbedding.forward / apply_rotary_emb
  *                                (dllmserve/layers/rotary_embedding.py:6-16, 41-57), the
  *                                op the decoder layers apply to q, k just before attention
+ *   dllm_attn_varlen_heads_fwd  attention for a list of query heads only (no reference
+ *                                counterpart: the head-level form of the sparse path)
  *   dllm_build_step_plan      <- the per-sequence metadata of attention.py:168-304 /
  *                                model_runner.py:240-321, on the device
  *   dllm_select_kv_store      <- _select_important_head_kv (attention.py:344-413) or
@@ -287,6 +289,29 @@ DLLM_API int dllm_select_kv_store(const void* q, int64_t q_tok_stride, const voi
                          int head_select, void* k_cache, void* v_cache, int64_t cache_tok_stride,
                          int64_t num_slots, const int32_t* slots, int64_t* top_idx,
                          int32_t* err_flag, void* stream);
+
+/*
+ * Head-compacted attention: dllm_attn_varlen_fwd (or, with k_cache/v_cache/slots/
+ * cu_seqlens_slots, dllm_attn_varlen_paged_fwd) computed only for the query heads
+ * head_idx[0 .. num_selected_heads) (device int32, each in [0, num_heads); with GQA the
+ * KV head of query head h is h / (num_heads / num_kv_heads)). Work units are numbered
+ * over the list, so heads left out cost nothing; their output rows are not written.
+ * An index outside [0, num_heads) sets DLLM_DEV_BAD_SEQUENCE in err_flag and its units
+ * are skipped. The slots / cu_seqlens_slots pair is optional (both null: no cached
+ * segment). No counterpart in the reference, which keeps every head and selects tokens
+ * per KV head (attention.py:344-413); this is the head-level form of the sparse path.
+ */
+DLLM_API int dllm_attn_varlen_heads_fwd(const void* q, int64_t q_tok_stride, const void* k,
+                                        int64_t k_tok_stride, const void* v, int64_t v_tok_stride,
+                                        const void* k_cache, const void* v_cache,
+                                        int64_t cache_tok_stride, int64_t num_slots,
+                                        const int32_t* slots, const int32_t* cu_seqlens_slots, void* o,
+                                        int64_t o_tok_stride, const int32_t* cu_seqlens_q,
+                                        const int32_t* cu_seqlens_k, int batch, int max_seqlen_q,
+                                        int64_t total_q, int64_t total_k, int num_heads, int num_kv_heads,
+                                        int head_dim, float softmax_scale, const int32_t* head_idx,
+                                        int num_selected_heads, int32_t* sched_workspace, int32_t* err_flag,
+                                        void* stream);
 
 /*
  * Per-step metadata of the diffusion attention path, built on the device in one
