@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 OUT = os.path.join(HERE, "dllmserve_b200", "libdllm_attn.so")
 SOURCES = ["attn_fwd.cu", "attn_fwd_split.cu", "kvcache.cu", "select_kv.cu", "rope.cu", "step_plan.cu",
-           "capi.cu"]
+           "oproj_ar.cu", "capi.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -13,6 +13,7 @@
 #include "select_kv.h"
 #include "rope.h"
 #include "step_plan.h"
+#include "oproj_ar.h"
 
 namespace {
 
@@ -87,6 +88,39 @@ int encode_rows_map(CUtensorMap* m, const void* ptr, int64_t rows, int heads, in
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(DLLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return DLLM_OK;
+}
+
+// 2-D map over a row-major bf16 matrix [rows, cols] (row stride in elements):
+// box (64 columns, box_rows rows), 128-byte swizzle (UMMA SW128 K-major).
+int encode_matrix_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t row_stride,
+                      int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return fail(DLLM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DLLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DLLM_OK;
+}
+
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+GetAddressRangeFn get_address_range_fn() {
+  static std::atomic<GetAddressRangeFn> fn{nullptr};
+  GetAddressRangeFn f = fn.load();
+  if (f == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f = reinterpret_cast<GetAddressRangeFn>(p);
+    fn.store(f);
+  }
+  return f;
 }
 
 int check_rows(const char* name, const void* p, int64_t tok_stride, int heads, int64_t rows) {
@@ -560,6 +594,83 @@ int dllm_build_step_plan(const int64_t* seqs, int batch, int num_kv_heads, int32
   a.err = err_flag;
   cudaError_t e = dllm::launch_step_plan(a, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "step plan launch");
+  return DLLM_OK;
+}
+
+int dllm_oproj_allreduce(const void* x, int64_t x_stride, const void* w, int64_t w_stride, int M, int N,
+                         int K, void* const* recv, void* const* y, int32_t* const* flags, int rank,
+                         int tp, int epoch, int32_t* err_flag, void* stream) {
+  if (tp < 1 || tp > DLLM_OPROJ_MAX_RANKS || rank < 0 || rank >= tp)
+    return fail(DLLM_ERR_INVALID_ARG, "rank %d / tp %d (tp must be 1..%d)", rank, tp, DLLM_OPROJ_MAX_RANKS);
+  if (M < 0 || N <= 0 || K <= 0) return fail(DLLM_ERR_INVALID_ARG, "bad sizes M=%d N=%d K=%d", M, N, K);
+  if (N % 256 != 0 || K % 64 != 0)
+    return fail(DLLM_ERR_UNSUPPORTED, "N %% 256 == 0 and K %% 64 == 0 required (N=%d K=%d)", N, K);
+  if (epoch == 0) return fail(DLLM_ERR_INVALID_ARG, "epoch must be nonzero (flags start at 0)");
+  if (M == 0) return DLLM_OK;
+  if (!x || !w || !recv || !y || !flags) return fail(DLLM_ERR_INVALID_ARG, "null pointer");
+  if (!aligned(x, 16) || !aligned(w, 16) || x_stride % 8 || w_stride % 8 || x_stride < K || w_stride < K)
+    return fail(DLLM_ERR_ALIGNMENT, "x / w must be 16-byte aligned with row strides %% 8 == 0 and >= K");
+  dllm::OprojArArgs a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.rank = rank;
+  a.tp = tp;
+  a.epoch = epoch;
+  a.tiles_m = (M + 127) / 128;
+  a.tiles_n = N / 256;
+  const int64_t tiles = (int64_t)a.tiles_m * a.tiles_n;
+  if (tiles >= ((int64_t)1 << 30)) return fail(DLLM_ERR_TOO_LARGE, "too many tiles");
+  a.num_tiles = (int)tiles;
+  for (int p = 0; p < tp; ++p) {
+    if (!recv[p] || !y[p] || !flags[p]) return fail(DLLM_ERR_INVALID_ARG, "null buffer of rank %d", p);
+    if (!aligned(recv[p], 16) || !aligned(y[p], 16) || !aligned(flags[p], 4))
+      return fail(DLLM_ERR_ALIGNMENT, "buffers of rank %d misaligned", p);
+    a.recv[p] = reinterpret_cast<__nv_bfloat16*>(recv[p]);
+    a.y[p] = reinterpret_cast<__nv_bfloat16*>(y[p]);
+    a.flags[p] = flags[p];
+  }
+  a.err = err_flag;
+  CUtensorMap tmA, tmB;
+  int rc;
+  if ((rc = encode_matrix_map(&tmA, x, M, K, x_stride, 128)) != DLLM_OK) return rc;
+  if ((rc = encode_matrix_map(&tmB, w, N, K, w_stride, 256)) != DLLM_OK) return rc;
+  cudaError_t e = dllm::launch_oproj_ar(tmA, tmB, a, num_sms_of_current_device(),
+                                        reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "oproj_allreduce launch");
+  return DLLM_OK;
+}
+
+int dllm_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return fail(DLLM_ERR_INVALID_ARG, "null pointer");
+  GetAddressRangeFn range = get_address_range_fn();
+  if (range == nullptr) return fail(DLLM_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  CUdeviceptr b = 0;
+  size_t size = 0;
+  CUresult r = range(&b, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(DLLM_ERR_CUDA, "cuMemGetAddressRange failed (%d)", (int)r);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(b));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) <= DLLM_IPC_HANDLE_BYTES, "handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)(reinterpret_cast<CUdeviceptr>(ptr) - b);
+  return DLLM_OK;
+}
+
+int dllm_ipc_open(const void* handle, void** base) {
+  if (handle == nullptr || base == nullptr) return fail(DLLM_ERR_INVALID_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return DLLM_OK;
+}
+
+int dllm_ipc_close(void* base) {
+  if (base == nullptr) return DLLM_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
   return DLLM_OK;
 }
 

@@ -192,6 +192,48 @@ DLLM_DEVICE void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int c
       : "memory");
 }
 
+// 2-D tiled load (coordinates: innermost first), completes tx bytes on `bar`.
+// No multicast; the tensor map covers this GPU's own memory.
+DLLM_DEVICE void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1,
+                             uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "l"(cache_hint)
+      : "memory");
+}
+
+// System-scope flag access (flags written by another GPU over NVLink).
+DLLM_DEVICE int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+DLLM_DEVICE void st_release_sys(int32_t* p, int32_t v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Barrier among `count` threads (whole warps) on hardware barrier `id` (1..15).
+DLLM_DEVICE void named_barrier(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Barrier among `count` threads on hardware barrier `id` that also returns
+// whether `pred` held for every one of them: warps that took a bounded wait
+// agree on its outcome before any of them leaves a loop with barriers in it.
+DLLM_DEVICE bool named_barrier_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // L2 eviction policies (createpolicy) for TMA cache hints.
 DLLM_DEVICE uint64_t policy_evict_last() {
   uint64_t p;

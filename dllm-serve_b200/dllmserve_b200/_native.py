@@ -26,6 +26,8 @@ SEQ_DESC_INTS = 8
 PLAN_SEQ_FIELDS = 10   # DLLM_PLAN_SEQ_FIELDS
 PLAN_LAYOUT_INTS = 12  # DLLM_PLAN_LAYOUT_INTS
 PLAN_MAX_BATCH = 1024  # DLLM_PLAN_MAX_BATCH
+OPROJ_MAX_RANKS = 8    # DLLM_OPROJ_MAX_RANKS
+IPC_HANDLE_BYTES = 64  # DLLM_IPC_HANDLE_BYTES
 SCHED_WORKSPACE_INTS = 2  # DLLM_SCHED_WORKSPACE_INTS
 
 # Every exported entry point with its (argtypes, restype).
@@ -71,6 +73,10 @@ SIGNATURES = {
         _I,
     ),
     "dllm_build_step_plan": ([_P, _I, _I, _P, _P, _P, _P], _I),
+    "dllm_oproj_allreduce": ([_P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _I, _I, _I, _P, _P], _I),
+    "dllm_ipc_export": ([_P, _P, _P], _I),
+    "dllm_ipc_open": ([_P, _P], _I),
+    "dllm_ipc_close": ([_P], _I),
     "dllm_select_kv_store": (
         [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I64, _I64, _P, _P, _P, _P],
         _I,

@@ -27,6 +27,8 @@
  *                                op the decoder layers apply to q, k just before attention
  *   dllm_attn_varlen_heads_fwd  attention for a list of query heads only (no reference
  *                                counterpart: the head-level form of the sparse path)
+ *   dllm_oproj_allreduce      <- RowParallelLinear.forward: F.linear + dist.all_reduce
+ *                                (linear.py:186-190), one kernel over NVLink peer memory
  *   dllm_build_step_plan      <- the per-sequence metadata of attention.py:168-304 /
  *                                model_runner.py:240-321, on the device
  *   dllm_select_kv_store      <- _select_important_head_kv (attention.py:344-413) or
@@ -346,6 +348,43 @@ DLLM_API int dllm_attn_varlen_heads_fwd(const void* q, int64_t q_tok_stride, con
 #define DLLM_PLAN_MAX_BATCH 1024
 DLLM_API int dllm_build_step_plan(const int64_t* seqs, int batch, int num_kv_heads, int32_t* out,
                                   const int64_t* layout, int32_t* err_flag, void* stream);
+
+/*
+ * Row-parallel o_proj fused with its all-reduce over NVLink peer memory
+ * (replaces RowParallelLinear.forward: F.linear then dist.all_reduce,
+ * linear.py:186-190). Every rank r of a tp-way group calls it, in the same order
+ * and with the same epoch, for its x_r [M, K] (bf16, row stride x_stride) and
+ * W_r [N, K] (its column slice of W_o, bf16, row stride w_stride); afterwards
+ * y[rank] holds y = sum_r x_r W_r^T [M, N] (bf16; fp32 GEMM accumulation, each
+ * rank's partial rounded to bf16, partials summed in rank order in fp32 and
+ * rounded once). recv[p], y[p], flags[p] (HOST arrays of tp device pointers) are
+ * rank p's buffers as addressed from this rank (its own, or a mapping of the
+ * peer's from dllm_ipc_open): recv [tp, M, N] bf16 receive buffer, y [M, N] bf16
+ * output, flags int32 [(tp + 1) * ceil(M/128) * N/256], zero before the first call.
+ * epoch: nonzero, distinct from the previous call's (a counter). A rank can run at
+ * most one call ahead of its peers, so alternate two y buffers between calls if
+ * the output of a call is read after the next call started on a peer.
+ * Bounded waits: a peer that does not take part makes the call end with
+ * DLLM_DEV_WAIT_TIMEOUT in err_flag. N % 256 == 0, K % 64 == 0, tp <= 8.
+ * No multicast, and no TMA or library code reads peer memory.
+ */
+#define DLLM_OPROJ_MAX_RANKS 8
+DLLM_API int dllm_oproj_allreduce(const void* x, int64_t x_stride, const void* w, int64_t w_stride,
+                                  int M, int N, int K, void* const* recv, void* const* y,
+                                  int32_t* const* flags, int rank, int tp, int epoch,
+                                  int32_t* err_flag, void* stream);
+
+/*
+ * CUDA IPC for the buffers of dllm_oproj_allreduce: dllm_ipc_export writes the
+ * handle (DLLM_IPC_HANDLE_BYTES) of the allocation holding `ptr` and ptr's offset in
+ * it; a peer process opens it with dllm_ipc_open (base address of the mapping; add
+ * the offset) and releases it with dllm_ipc_close. These map memory the peer
+ * owns; they allocate nothing.
+ */
+#define DLLM_IPC_HANDLE_BYTES 64
+DLLM_API int dllm_ipc_export(const void* ptr, void* handle, int64_t* offset);
+DLLM_API int dllm_ipc_open(const void* handle, void** base);
+DLLM_API int dllm_ipc_close(void* base);
 
 #ifdef __cplusplus
 }

@@ -5,7 +5,9 @@ dllmserve/layers/linear.py:55-88, with the per-rank cache slice of
 model_runner.py:174). Checked per rank: its launch equals the single-launch
 result on those heads bit for bit and the fp32 oracle within tolerance; the
 all-reduced row-parallel o_proj (linear.py:186-190) equals the single-GPU
-o_proj within bf16 tolerance."""
+o_proj within bf16 tolerance, both through NCCL after the GEMM and through
+the fused kernel that pushes GEMM tiles over NVLink (dllm_oproj_allreduce),
+whose result is also identical on both ranks, call after call."""
 import datetime
 import os
 import socket
@@ -71,6 +73,19 @@ def _worker(rank, world, port, hq, hkv, lens, hidden, out_path):
         torch.cuda.synchronize()
         e = (y.float() - y_ref.float()).abs()
         res["oproj_err"] = (float(e.max()), float(e.mean()), float(y_ref.float().abs().mean()))
+        from dllmserve_b200.tp import OprojAllReduce
+
+        fused = OprojAllReduce(part.shape[0], hidden, device=dev)
+        ys = []
+        for _ in range(3):
+            yf = fused(part.reshape(part.shape[0], -1), wd[:, h0 * D:h1 * D].contiguous())
+            torch.cuda.synchronize()
+            ys.append(yf.clone())
+        fused.close()
+        e = (ys[-1].float() - y_ref.float()).abs()
+        res["fused_err"] = (float(e.max()), float(e.mean()))
+        res["fused_repeat_equal"] = all(torch.equal(ys[0], yy) for yy in ys[1:])
+        res["fused_y"] = ys[-1].cpu()
         res["status"] = ops.read_device_status(dev)
     finally:
         torch.save(res, f"{out_path}.{rank}")
@@ -91,4 +106,8 @@ def test_head_sharded_tp_on_two_gpus(tmp_path, hq, hkv, lens):
         assert res["oracle_err"][0] <= 2e-2 and res["oracle_err"][1] <= 2e-3, res["oracle_err"]
         mx, mean, scale = res["oproj_err"]
         assert mx <= 2e-2 and mean <= 2e-3 * max(1.0, scale), res["oproj_err"]
+        assert res["fused_err"][0] <= 2e-2 and res["fused_err"][1] <= 2e-3 * max(1.0, scale), res["fused_err"]
+        assert res["fused_repeat_equal"]
         assert res["status"] == 0
+    y0, y1 = (torch.load(f"{out}.{r}")["fused_y"] for r in range(world))
+    assert torch.equal(y0, y1)
