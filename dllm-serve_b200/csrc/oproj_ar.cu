@@ -14,12 +14,13 @@
 //      (owner = tile index mod tp; plain stores through an IPC mapping of the
 //      owner's memory, or local), then raises the tile's flag on the owner
 //      (system-scope release, value = this call's epoch).
-//   B) For each tile it owns, the rank waits for the tp partials (bounded),
-//      sums them in rank order in fp32, rounds once to bf16 and writes the
-//      result to every rank's output (plain peer stores), then raises the
-//      tile's final flag on every other rank.
+//   B) Meanwhile two warps of each CTA take the tiles the rank owns: they
+//      wait for the tp partials (bounded), sum them in rank order in fp32,
+//      round once to bf16 and write the result to every rank's output (plain
+//      peer stores), then raise the tile's final flag on every other rank.
 //   C) The rank waits for the final flags of the tiles it does not own, so
 //      its output is complete when the kernel ends.
+// With tp == 1 the epilogue writes the result directly (a plain GEMM).
 // Phase A waits on nothing outside the GPU, so no cycle of waits exists
 // across ranks; every wait is bounded (kWaitLimitNs) and a timeout anywhere
 // raises DLLM_DEV_WAIT_TIMEOUT in the status word, which every other wait
@@ -33,19 +34,20 @@ namespace dllm {
 namespace {
 
 constexpr int kTM = 128, kTN = 256, kTK = 64;
-constexpr int kStages = 3;
+constexpr int kStages = 4;
 constexpr uint32_t kABytes = kTM * kTK * 2;                 // 16 KB
 constexpr uint32_t kBBytes = kTN * kTK * 2;                 // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;         // 48 KB
-constexpr uint32_t kOffOut = kStages * kStageBytes;         // bf16 tile staging, 64 KB
-constexpr uint32_t kOutBytes = kTM * kTN * 2;
+constexpr uint32_t kOffOut = kStages * kStageBytes;         // bf16 staging of half a tile, 32 KB
+constexpr uint32_t kOutBytes = kTM * (kTN / 2) * 2;
 constexpr uint32_t kOffBar = kOffOut + kOutBytes;
 constexpr int BAR_FULL = 0, BAR_EMPTY = kStages, BAR_ACCF = 2 * kStages, BAR_ACCE = 2 * kStages + 2;
 constexpr int BAR_DRAIN = 2 * kStages + 4;
 constexpr int kNumBars = 2 * kStages + 5;
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;       // + alignment slack
-constexpr int kThreads = 256;  // warp 0 TMA, warp 1 MMA, warps 4-7 epilogue; all reduce
+constexpr int kThreads = 256;  // warp 0 TMA, warp 1 MMA, warps 2-3 reduce, warps 4-7 epilogue
+constexpr int kReduceBatch = 8;  // 16-byte vectors in flight per reducing thread
 
 // Spin (bounded) until *flag == epoch. False on timeout or when another CTA of
 // this GPU gave up (status word set); a timeout sets the status word.
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp >= 4) {
+    // ------------------------------------------------------ epilogue (A)
     const int wq = warp & 3;
     const int rr = wq * 32 + lane;  // tile row held by this thread (TMEM lane)
     uint4* stage_out = reinterpret_cast<uint4*>(smem + kOffOut);
@@ -177,87 +180,116 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = named_barrier_and(1, 128, ok);
       if (!ok) break;
       tc_fence_after();
-      // TMEM -> bf16 -> staging (row rr: 32 chunks of 16 B, chunk j at j ^ (rr & 7))
+      // tp == 1: the tile is the result; else the partial goes to its owner
+      const int owner = t % a.tp;
+      __nv_bfloat16* dst = a.tp == 1
+                               ? a.y[0] + (int64_t)(tm * kTM) * a.N + tn * kTN
+                               : a.recv[owner] + (int64_t)a.rank * MN + (int64_t)(tm * kTM) * a.N + tn * kTN;
+      for (int h = 0; h < 2; ++h) {
+        // TMEM -> bf16 -> staging (row rr: 16 chunks of 16 B, chunk j at j ^ (rr & 7))
 #pragma unroll 1
-      for (int c = 0; c < kTN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + buf * kTN + c * 32, v);
-        tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + buf * kTN + h * (kTN / 2) + c * 32, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
-          w.y = pack_bf16x2(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
-          w.z = pack_bf16x2(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
-          w.w = pack_bf16x2(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
-          const int j = c * 4 + q;
-          stage_out[rr * 32 + (j ^ (rr & 7))] = w;
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
+            w.y = pack_bf16x2(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
+            w.z = pack_bf16x2(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
+            w.w = pack_bf16x2(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
+            const int j = c * 4 + q;
+            stage_out[rr * 16 + (j ^ (rr & 7))] = w;
+          }
+        }
+        if (h == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(BAR_ACCE + buf));  // TMEM buffer free for the next tile
+        }
+        named_barrier(1, 128);
+        // staging -> destination: two 256-byte row halves per warp step
+        for (int i = wq * 32 + lane; i < kTM * 16; i += 128) {
+          const int r = i >> 4, ch = i & 15;
+          if (tm * kTM + r >= a.M) break;
+          reinterpret_cast<uint4*>(dst + (int64_t)r * a.N + h * (kTN / 2))[ch] = stage_out[r * 16 + (ch ^ (r & 7))];
+        }
+        named_barrier(1, 128);  // staging read before the next half overwrites it
+      }
+      if (a.tp > 1) {
+        __threadfence_system();
+        named_barrier(1, 128);
+        if (wq == 0 && lane == 0) st_release_sys(a.flags[owner] + (int64_t)a.rank * a.num_tiles + t, a.epoch);
+      }
+    }
+  } else if (a.tp > 1) {
+    // -------------------------------------- warps 2-3: reduction (B), overlapping A
+    // Tiles owned by this rank, t = rank + tp * k for k = blockIdx.x,
+    // blockIdx.x + gridDim.x, ...: wait for the tp partials, sum them in rank
+    // order, push the result to every rank, raise the final flags.
+    const int tid = threadIdx.x - 64;
+    const int64_t fin = (int64_t)a.tp * a.num_tiles;
+    const __nv_bfloat16* own = a.recv[a.rank];
+    bool ok = true;
+    for (int t = a.rank + a.tp * (int)blockIdx.x; t < a.num_tiles && ok; t += a.tp * (int)gridDim.x) {
+      bool got = true;
+      if (tid == 0)
+        for (int src = 0; src < a.tp && got; ++src)
+          got = wait_flag(a.flags[a.rank] + (int64_t)src * a.num_tiles + t, a.epoch, a.err);
+      ok = named_barrier_and(2, 64, got);
+      if (!ok) break;
+      const int tm = t / a.tiles_n, tn = t - tm * a.tiles_n;
+      for (int v0 = tid; v0 < kTM * (kTN / 8); v0 += 64 * kReduceBatch) {
+        float acc[kReduceBatch][8];
+        int64_t off[kReduceBatch];
+        bool in[kReduceBatch];
+#pragma unroll
+        for (int b = 0; b < kReduceBatch; ++b) {
+          const int v = v0 + b * 64;
+          const int r = v / (kTN / 8), cc = v - r * (kTN / 8);
+          in[b] = v < kTM * (kTN / 8) && tm * kTM + r < a.M;
+          off[b] = (int64_t)(tm * kTM + r) * a.N + tn * kTN + cc * 8;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[b][e] = 0.f;
+        }
+        for (int src = 0; src < a.tp; ++src) {
+          uint4 w[kReduceBatch];
+#pragma unroll
+          for (int b = 0; b < kReduceBatch; ++b)
+            w[b] = in[b] ? __ldcg(reinterpret_cast<const uint4*>(own + (int64_t)src * MN + off[b]))
+                         : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int b = 0; b < kReduceBatch; ++b) {
+            float x[8];
+            bf16x8_to_f32(w[b], x);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[b][e] += x[e];
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kReduceBatch; ++b) {
+          if (!in[b]) continue;
+          uint4 o;
+          o.x = pack_bf16x2(acc[b][0], acc[b][1]);
+          o.y = pack_bf16x2(acc[b][2], acc[b][3]);
+          o.z = pack_bf16x2(acc[b][4], acc[b][5]);
+          o.w = pack_bf16x2(acc[b][6], acc[b][7]);
+          for (int p = 0; p < a.tp; ++p) *reinterpret_cast<uint4*>(a.y[p] + off[b]) = o;
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(BAR_ACCE + buf));  // TMEM buffer free for the next tile
-      named_barrier(1, 128);
-      // staging -> owner's receive buffer, one 512-byte row per warp step
-      const int owner = t % a.tp;
-      __nv_bfloat16* dst = a.recv[owner] + (int64_t)a.rank * MN + (int64_t)(tm * kTM) * a.N + tn * kTN;
-      for (int r = wq; r < kTM; r += 4) {
-        if (tm * kTM + r >= a.M) break;
-        const uint4 w = stage_out[r * 32 + (lane ^ (r & 7))];
-        reinterpret_cast<uint4*>(dst + (int64_t)r * a.N)[lane] = w;
-      }
       __threadfence_system();
-      named_barrier(1, 128);
-      if (wq == 0 && lane == 0) st_release_sys(a.flags[owner] + (int64_t)a.rank * a.num_tiles + t, a.epoch);
+      named_barrier(2, 64);
+      if (tid == 0)
+        for (int p = 0; p < a.tp; ++p)
+          if (p != a.rank) st_release_sys(a.flags[p] + fin + t, a.epoch);
     }
   }
-  // ------------------------------------------------------- phases B and C
-  tc_fence_before();
-  __syncthreads();
-  const int64_t fin = (int64_t)a.tp * a.num_tiles;  // final flags follow the partial flags
-  bool ok = *abort_flag == 0;
-  // B: tiles owned by this rank: t = rank + tp * k, k = blockIdx.x, blockIdx.x + gridDim.x, ...
-  for (int t = a.rank + a.tp * (int)blockIdx.x; t < a.num_tiles && ok; t += a.tp * (int)gridDim.x) {
-    if (threadIdx.x == 0) {
-      bool got = true;
-      for (int src = 0; src < a.tp && got; ++src)
-        got = wait_flag(a.flags[a.rank] + (int64_t)src * a.num_tiles + t, a.epoch, a.err);
-      *bcast = got ? 1 : 0;
-    }
-    __syncthreads();
-    ok = *bcast != 0;
-    __syncthreads();
-    if (!ok) break;
-    const int tm = t / a.tiles_n, tn = t - tm * a.tiles_n;
-    const __nv_bfloat16* own = a.recv[a.rank];
-    for (int v = threadIdx.x; v < kTM * (kTN / 8); v += kThreads) {
-      const int r = v / (kTN / 8), cc = v - r * (kTN / 8);
-      const int row = tm * kTM + r;
-      if (row >= a.M) continue;
-      const int64_t off = (int64_t)row * a.N + tn * kTN + cc * 8;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int src = 0; src < a.tp; ++src) {
-        const uint4 w = __ldcg(reinterpret_cast<const uint4*>(own + (int64_t)src * MN + off));
-        float x[8];
-        bf16x8_to_f32(w, x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += x[e];
-      }
-      uint4 o;
-      o.x = pack_bf16x2(acc[0], acc[1]);
-      o.y = pack_bf16x2(acc[2], acc[3]);
-      o.z = pack_bf16x2(acc[4], acc[5]);
-      o.w = pack_bf16x2(acc[6], acc[7]);
-      for (int p = 0; p < a.tp; ++p) *reinterpret_cast<uint4*>(a.y[p] + off) = o;
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0)
-      for (int p = 0; p < a.tp; ++p)
-        if (p != a.rank) st_release_sys(a.flags[p] + fin + t, a.epoch);
-  }
-  // C: final tiles of the other owners, spread over the CTAs
-  if (ok && threadIdx.x == 0) {
+  // ---------------------------------------------------------------- phase C
+  // Final tiles of the other owners, spread over the CTAs (thread 0, once
+  // this CTA's GEMM tiles are out).
+  if (a.tp > 1 && threadIdx.x == 0 && *abort_flag == 0) {
+    const int64_t fin = (int64_t)a.tp * a.num_tiles;
     for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
       if (t % a.tp == a.rank) continue;
       if (!wait_flag(a.flags[a.rank] + fin + t, a.epoch, a.err)) break;
