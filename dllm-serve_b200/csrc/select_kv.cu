@@ -244,9 +244,12 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     constexpr int kHalves = kThreads / 16;
     // The trip count is uniform over the warp (both halves step together), so
     // the 16-lane shuffle reductions always run with all 32 lanes.
-    for (int cw = 2 * warp; cw < Klen; cw += kHalves * kRowsInFlight) {
+    // Software-pipelined: the next batch's rows are requested before the
+    // current batch is scored, so every half warp keeps 2 x kRowsInFlight
+    // row loads outstanding instead of waiting a full memory latency per batch.
+    constexpr int kStride = kHalves * kRowsInFlight;
+    auto load_batch = [&](int cw, uint4 (&w)[kRowsInFlight]) {
       const int c0 = cw + (hw & 1);
-      uint4 w[kRowsInFlight];
 #pragma unroll
       for (int r = 0; r < kRowsInFlight; ++r) {
         const int c = c0 + r * kHalves;
@@ -257,6 +260,12 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
                                                       (int64_t)h * kD) + hl);
         }
       }
+    };
+    uint4 w[kRowsInFlight], wn[kRowsInFlight];
+    if (2 * warp < Klen) load_batch(2 * warp, w);
+    for (int cw = 2 * warp; cw < Klen; cw += kStride) {
+      if (cw + kStride < Klen) load_batch(cw + kStride, wn);
+      const int c0 = cw + (hw & 1);
 #pragma unroll
       for (int r = 0; r < kRowsInFlight; ++r) {
         float x[8];
@@ -280,6 +289,8 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
         const int c = c0 + r * kHalves;
         if (hl == 0 && c < Klen) scores[c] = __fdiv_rn(best, a.sqrt_d);
       }
+#pragma unroll
+      for (int r = 0; r < kRowsInFlight; ++r) w[r] = wn[r];
     }
   } else {
     // Shared ranking: sum over every query head h of q_avg[h] . k[c, h / group].
