@@ -918,8 +918,9 @@ def sparse_cycle(workload, steps, warmup):
 
 def run_kernels_case(args):
     """Small profiling case: each native kernel launched 3 times on inputs
-    larger than L2 (one c2 layer for attention, the KV store and RoPE, config-5
-    shapes for scoring/top-k and for the reuse-state attention)."""
+    larger than L2 (one c2 layer for attention, the KV store, RoPE and the
+    fused o_proj GEMM at tp=1, config-5 shapes for scoring/top-k and for the
+    reuse-state attention)."""
     from dllmserve_b200 import _native, ops
 
     _native.lib()
@@ -972,7 +973,18 @@ def run_kernels_case(args):
     for _ in range(3):
         ops.varlen_attention(q3, k3, v3, cq, cq, 32, k_cache=kc5, v_cache=vc5, slots=slot3,
                              cu_seqlens_slots=cc)
+    del q3, k3, v3, kc5, vc5
+    # row-parallel o_proj of one config-2 layer through the fused kernel on
+    # one rank (dllm_oproj_allreduce at tp=1: the GEMM with its direct epilogue)
+    from dllmserve_b200.tp import OprojAllReduce
+
+    x = rnd(N, HEADS * HEAD_DIM)
+    w = rnd(HIDDEN, HEADS * HEAD_DIM) * 0.02
+    fused = OprojAllReduce(N, HIDDEN, device=dev)
+    for _ in range(3):
+        fused(x, w)
     torch.cuda.synchronize()
+    fused.close()
     if ops.read_device_status(dev) != 0:
         raise RuntimeError("a kernel reported a device error")
     print(json.dumps({"kernels_case": "ok", "launches": ops.LAUNCHES[0]}))
