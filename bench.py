@@ -280,6 +280,103 @@ def run_reference_arm(args, lens):
     return 0
 
 
+def _cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_cpu_baselines(args):
+    """``--cpu-baselines``: the reference's CPU attention path on the host
+    cores for configs 1, 3, 4 and 5 (config 2 is the ``--impl reference``
+    arm): the reference's own ``Attention.forward`` (installed package under
+    baseline/_ref; flash-attn/Triton callees replaced by CPU stand-ins), fp32,
+    one layer per measurement on a bounded sample of each workload's
+    sequences (the same seeded prompt lengths as ``--workload``). Sparse
+    configs time a dense step, a compute-cache step (state 1: attention,
+    selection and cache store) and a reuse step (state 2) of that layer;
+    per-layer times are also extrapolated to the whole batch and all layers
+    (labelled as such). Prints one JSON line (rank 0 only)."""
+    import platform
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    try:
+        from oracle import reference_module as RM
+
+        R = RM.load()
+    except ImportError as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference package not installed: {e}"}))
+        return 0
+    budget = args.cpu_budget
+    scale = HEAD_DIM ** -0.5
+
+    def timed(fn):
+        fn()  # first call: allocations, lazy imports
+        t0, n = time.perf_counter(), 0
+        while True:
+            fn()
+            n += 1
+            if time.perf_counter() - t0 > budget / 3 or n >= 20:
+                return (time.perf_counter() - t0) / n
+
+    g = torch.Generator().manual_seed(7)
+    out = {"impl": "reference", "kind": "reference", "cores": cores, "cpu": _cpu_model(),
+           "host": platform.node(), "dtype": "f32",
+           "what": "the reference's dllmserve.layers.attention.Attention.forward on the host cores "
+                   "(installed package; flash-attn/Triton callees replaced by CPU stand-ins), one layer"}
+    # config 1: the whole config (one layer, one 64 + 32-token sequence, 32/32 heads)
+    q, k, v = (torch.randn(96, HEADS, HEAD_DIM, generator=g) for _ in range(3))
+    t = timed(lambda: RM.dense_layer_forward(R, q, k, v, [96], HEADS, HEADS, HEAD_DIM, scale))
+    out["c1"] = {"ms": t * 1e3, "tflops": attn_flops([96]) / t / 1e12,
+                 "sample": "the whole config: one layer, one sequence of 64 + 32 tokens, 32/32 heads x 128"}
+    for wl in ("c3", "c4", "c5"):
+        layers, Hq, Hkv, B, (plo, phi), gen, ratio, desc = SPARSE_WORKLOADS[wl]
+        gw = torch.Generator().manual_seed(40 + int(wl[1]))
+        prompts = torch.randint(plo, phi + 1, (B,), generator=gw).tolist()
+        lens = [p + gen for p in prompts]
+        # sample: the first n sequences, as many as fit the budget (probe with one)
+        probe = lens[:1]
+        qp, kp, vp = (torch.randn(sum(probe), h, HEAD_DIM, generator=g) for h in (Hq, Hkv, Hkv))
+        t0 = time.perf_counter()
+        RM.dense_layer_forward(R, qp, kp, vp, probe, Hq, Hkv, HEAD_DIM, scale)
+        per_flop = (time.perf_counter() - t0) / attn_flops(probe, Hq)
+        n = 1
+        while n < B and per_flop * attn_flops(lens[:n + 1], Hq) < budget / 6:
+            n += 1
+        sl, sp = lens[:n], prompts[:n]
+        N = sum(sl)
+        q, k, v = (torch.randn(N, h, HEAD_DIM, generator=g) for h in (Hq, Hkv, Hkv))
+        t_dense = timed(lambda: RM.dense_layer_forward(R, q, k, v, sl, Hq, Hkv, HEAD_DIM, scale))
+        cyc = RM.SparseLayerCycle(R, sp, gen, Hq, Hkv, HEAD_DIM, ratio, True)
+        t_state = {}
+        for st in (1, 2):  # state 1 fills the cache that state 2 reads
+            rows = cyc.rows(st)
+            qs_, ks_, vs_ = (torch.randn(rows, h, HEAD_DIM, generator=g) for h in (Hq, Hkv, Hkv))
+            t_state[st] = timed(lambda: cyc.forward(st, qs_, ks_, vs_))
+        full = attn_flops(lens, Hq) / attn_flops(sl, Hq)  # dense / state-1 work scales with sum L^2
+        out[wl] = {
+            "desc": desc, "sample": f"{n} of {B} sequences (lengths {sl}), 1 of {layers} layers",
+            "dense_ms_per_layer": t_dense * 1e3, "dense_tflops": attn_flops(sl, Hq) / t_dense / 1e12,
+            "state1_ms_per_layer": t_state[1] * 1e3, "state2_ms_per_layer": t_state[2] * 1e3,
+            "n_keep": cyc.n_keep,
+            "extrapolated_full_step_ms": {"dense": t_dense * full * layers * 1e3,
+                                          "state1": t_state[1] * full * layers * 1e3,
+                                          "state2": t_state[2] * (B / n) * layers * 1e3,
+                                          "note": f"x {layers} layers; dense and state 1 scaled by the batch's "
+                                                  "sum L^2, state 2 by the sequence count"},
+        }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -1004,6 +1101,10 @@ def main():
                     help="c2 = the headline dense step; c3/c4/c5 = sparse diffusion-block cycle")
     ap.add_argument("--kernels-case", action="store_true",
                     help="run each native kernel 3x on a small case (for ncu captures)")
+    ap.add_argument("--cpu-baselines", action="store_true",
+                    help="time the reference's CPU path for configs 1, 3, 4 and 5 (one JSON line)")
+    ap.add_argument("--cpu-budget", type=float, default=6.0,
+                    help="seconds of CPU time per --cpu-baselines measurement")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (32 = the workload; fewer only for profiling runs)")
     args = ap.parse_args()
@@ -1011,6 +1112,8 @@ def main():
     lens = workload_lengths()
     if args.kernels_case:
         return run_kernels_case(args)
+    if args.cpu_baselines:
+        return run_cpu_baselines(args)
     if args.workload != "c2" and args.impl == "ours":
         return run_sparse_cycle(args)
     if args.impl == "reference":

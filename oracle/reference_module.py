@@ -124,3 +124,60 @@ def dense_layer_forward(R, q, k, v, lens, num_heads, num_kv_heads, head_dim, sca
         return layer(q.reshape(q.shape[0], -1), k.reshape(k.shape[0], -1), v.reshape(v.shape[0], -1))
     finally:
         R.ctx.reset_context()
+
+
+class SparseLayerCycle:
+    """One layer of the reference's ``Attention`` driven through a diffusion
+    block of head-sparse sequences on CPU, as the model runner drives it
+    (model_runner.py:240-321 builds the Context; attention.py:168-304
+    dispatches per sequence): every sequence at block 0 of its generation,
+    state 1 (compute cache: attention over the whole sequence, then
+    _select_important_head_kv / _select_important_kv and store_kvcache of the
+    selected rows, attention.py:204-233) and state 2 (reuse: the block's rows
+    attend to the cached selection plus the block, attention.py:235-265).
+
+    Inputs are fp32 [tokens, heads, head_dim]; state-1 inputs cover whole
+    sequences, state-2 inputs the blocks only (``rows(state)`` gives the
+    count)."""
+
+    def __init__(self, R, prompts, gen_len, num_heads, num_kv_heads, head_dim, retention_ratio,
+                 head_select, block_len=32, pool_kernel=3):
+        self.R = R
+        cfg = R.SparseConfig(enabled=True, default_block_len=block_len, retention_ratio=retention_ratio,
+                             pool_kernel=pool_kernel, delay_step=1, head_select=head_select)
+        cfg_model = types.SimpleNamespace(model_type=None, torch_device=torch.device("cpu"),
+                                          hf_config=types.SimpleNamespace(mask_token_id=0))
+        self.seqs, self.slots, page = [], [], 0
+        for p in prompts:
+            s = R.Sequence([1] * p, types.SimpleNamespace(gen_length=gen_len), cfg_model, cfg)
+            s.sparse_state.current_block_idx = 0
+            s.sparse_state.cache_state = 1
+            n = s.current_sparse_token
+            self.slots.append(torch.arange(page * 256, page * 256 + n, dtype=torch.int32))
+            page += (n + 255) // 256
+            self.seqs.append(s)
+        self.layer = R.att.Attention(num_heads, head_dim, head_dim ** -0.5, num_kv_heads, causal=False)
+        self.layer.k_cache = torch.zeros(max(page, 1), 256, num_kv_heads, head_dim)
+        self.layer.v_cache = torch.zeros(max(page, 1), 256, num_kv_heads, head_dim)
+        self.n_keep = [s.current_sparse_token for s in self.seqs]
+
+    def rows(self, state):
+        if state == 1:
+            return sum(s.num_tokens for s in self.seqs)
+        return sum(s.sparse_state.compute_block_boundaries(s.num_prompt_tokens, s.num_tokens)[1]
+                   for s in self.seqs)
+
+    def forward(self, state, q, k, v):
+        for s in self.seqs:
+            s.sparse_state.cache_state = state
+        cu = [0]
+        for s in self.seqs:
+            n = (s.num_tokens if state == 1 else
+                 s.sparse_state.compute_block_boundaries(s.num_prompt_tokens, s.num_tokens)[1])
+            cu.append(cu[-1] + n)
+        self.R.ctx.set_context(is_prefill=True, cu_seqlens_k=torch.tensor(cu, dtype=torch.int32),
+                               is_diffusion=True, seqs=self.seqs, slot_mapping=self.slots)
+        try:
+            return self.layer(q.reshape(q.shape[0], -1), k.reshape(k.shape[0], -1), v.reshape(v.shape[0], -1))
+        finally:
+            self.R.ctx.reset_context()

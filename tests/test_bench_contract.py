@@ -52,3 +52,29 @@ def test_reference_arm_other_ranks_exit_quietly(monkeypatch):
     with contextlib.redirect_stdout(out):
         assert bench.run_reference_arm(argparse.Namespace(gpus=2, steps=1, warmup=0), [64]) == 0
     assert out.getvalue() == ""
+
+
+def test_cpu_baselines_json(monkeypatch):
+    """``bench.py --cpu-baselines`` on shrunken workloads: one JSON line with
+    config 1 and, for each sparse config, the dense / compute-cache / reuse
+    per-layer times of the reference module (or an ``unavailable`` line when
+    the reference package is not installed)."""
+    monkeypatch.setenv("RANK", "0")
+    tiny = {"c3": (2, 4, 4, 2, (64, 64), 32, 0.5, "tiny c3"),
+            "c4": (2, 4, 2, 2, (40, 72), 32, 0.5, "tiny c4"),
+            "c5": (2, 4, 4, 1, (96, 96), 32, 0.25, "tiny c5")}
+    monkeypatch.setattr(bench, "SPARSE_WORKLOADS", tiny)
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out):
+        assert bench.run_cpu_baselines(argparse.Namespace(cpu_budget=0.05)) == 0
+    line = json.loads(out.getvalue().strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    if "unavailable" in line:
+        return
+    assert line["cores"] >= 1 and line["c1"]["tflops"] > 0
+    for wl in ("c3", "c4", "c5"):
+        r = line[wl]
+        for key in ("dense_ms_per_layer", "state1_ms_per_layer", "state2_ms_per_layer"):
+            assert r[key] > 0, (wl, key)
+        assert set(r["extrapolated_full_step_ms"]) >= {"dense", "state1", "state2"}
+        assert all(n >= 1 for n in r["n_keep"])
