@@ -79,6 +79,7 @@ class OprojAllReduce:
         if hidden % 256:
             raise ValueError("hidden must be a multiple of 256")
         self.distributed = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
+        self._group = group
         self.world = dist.get_world_size(group) if self.distributed else 1
         self.rank = dist.get_rank(group) if self.distributed else 0
         if self.world > _native.OPROJ_MAX_RANKS:
@@ -138,7 +139,9 @@ class OprojAllReduce:
             raise ValueError("x and w_shard must be bfloat16 with contiguous rows")
         if x.device != self.device or w_shard.device != self.device:
             raise ValueError(f"x and w_shard must be on {self.device}")
-        self.epoch = self.epoch + 1 if self.epoch < 0x7FFFFFF0 else 1
+        if self.epoch >= 0x7FFFFFF0:
+            self._reset_flags()
+        self.epoch += 1
         parity = self.epoch & 1
         lib = _native.lib()
         with torch.cuda.device(self.device):
@@ -149,6 +152,20 @@ class OprojAllReduce:
         ops.LAUNCHES[0] += 1
         start = self._off_y[parity]
         return self.buf[start:start + M * self.hidden * 2].view(torch.bfloat16).view(M, self.hidden)
+
+    def _reset_flags(self) -> None:
+        """Before the epoch counter wraps: every rank zeroes its own flags once
+        all ranks' kernels have finished (a flag left from an old call would
+        otherwise equal a new epoch), then the ranks meet again before any
+        writes the new epoch's flags. A collective over the group."""
+        torch.cuda.synchronize(self.device)
+        if self.distributed:
+            dist.barrier(group=self._group)
+        self.buf[self._off_flags:].zero_()
+        torch.cuda.synchronize(self.device)
+        if self.distributed:
+            dist.barrier(group=self._group)
+        self.epoch = 0
 
     def close(self) -> None:
         """Unmaps the peers' buffers (collective use must have ended)."""

@@ -67,3 +67,29 @@ def test_missing_peer_times_out_with_status():
     y = torch.ones(4, device=dev) * 2
     assert float(y.sum()) == 8.0
     ops.read_device_status(dev)
+
+
+def test_epoch_wraps_with_flag_reset():
+    """The epoch counter restarts at 1 after a collective flag reset (a flag
+    left from an old call must never equal a new epoch); results stay right
+    and the output buffers keep alternating across the wrap."""
+    from dllmserve_b200.tp import OprojAllReduce
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    M, N, K = 200, 512, 256
+    x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    w = (torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.05).to(torch.bfloat16)
+    ref = torch.nn.functional.linear(x, w).float()
+    fused = OprojAllReduce(M, N, device=dev)
+    fused.epoch = 0x7FFFFFF0 - 1
+    y0 = fused(x, w).clone()  # epoch 0x7FFFFFF0
+    assert fused.epoch == 0x7FFFFFF0
+    p0 = fused(x, w).data_ptr()  # reset, epoch 1
+    assert fused.epoch == 1
+    y1 = fused(x, w)  # epoch 2
+    torch.cuda.synchronize()
+    assert p0 != y1.data_ptr()
+    for y in (y0, y1):
+        assert (y.float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+    fused.close()
