@@ -335,18 +335,27 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   if (kHeadSelect || crank == 0) {
 
   // 3) max_pool1d(kernel=pool_k, stride 1, padding pool_k/2)[:Klen]
-  //    (attention.py:386-393 / :328-335), evaluated where it is read, as
-  //    order-preserving bits.
+  //    (attention.py:386-393 / :328-335), as order-preserving bits, computed
+  //    once: into the (still unused) selection buffer, then copied over the
+  //    raw scores, which nothing reads afterwards; every later pass reads one
+  //    word per key.
   const int pad = pool_k / 2;
-  auto pooled = [&](int c) -> uint32_t {
-    float m = scores[c];
-    if (pool_k > 1) {
-      const int lo = max(0, c - pad), hi = min(Klen - 1, c - pad + pool_k - 1);
-      m = -INFINITY;
-      for (int j = lo; j <= hi; ++j) m = fmaxf(m, scores[j]);
+  uint32_t* pbits = reinterpret_cast<uint32_t*>(scores);
+  {
+    uint32_t* tmp = reinterpret_cast<uint32_t*>(sel);  // 2 * p2max >= Klen words
+    for (int c = threadIdx.x; c < Klen; c += kThreads) {
+      float m = scores[c];
+      if (pool_k > 1) {
+        const int lo = max(0, c - pad), hi = min(Klen - 1, c - pad + pool_k - 1);
+        m = -INFINITY;
+        for (int j = lo; j <= hi; ++j) m = fmaxf(m, scores[j]);
+      }
+      tmp[c] = order_bits(m);
     }
-    return order_bits(m);
-  };
+    __syncthreads();
+    for (int c = threadIdx.x; c < Klen; c += kThreads) pbits[c] = tmp[c];
+    __syncthreads();
+  }
 
   int p2k = 1;
   while (p2k < Klen) p2k <<= 1;
@@ -361,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     __syncthreads();
     for (int cb = warp * 32; cb < Klen; cb += kThreads) {  // warp-uniform trip count
       const int c = cb + lane;
-      const uint32_t v = c < Klen ? pooled(c) : 0u;
+      const uint32_t v = c < Klen ? pbits[c] : 0u;
       const bool match = c < Klen && (v & mask) == prefix;
       const uint32_t active = __ballot_sync(0xffffffffu, match);
       if (match) {
@@ -412,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
     const uint32_t lt_mask = (1u << lane) - 1u;
     for (int c0 = 0; c0 < Klen; c0 += kThreads) {
       const int c = c0 + threadIdx.x;
-      const uint32_t v = c < Klen ? pooled(c) : 0u;
+      const uint32_t v = c < Klen ? pbits[c] : 0u;
       const bool gt = c < Klen && v > T;
       const bool eq = c < Klen && v == T;
       const uint32_t be = __ballot_sync(0xffffffffu, eq);
