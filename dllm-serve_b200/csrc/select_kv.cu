@@ -261,6 +261,9 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
         }
       }
     };
+    // the lane's 8 query-mean values of the group's first head stay in registers
+    const float4 qa0 = reinterpret_cast<const float4*>(q_avg)[2 * hl];
+    const float4 qb0 = reinterpret_cast<const float4*>(q_avg)[2 * hl + 1];
     uint4 w[kRowsInFlight], wn[kRowsInFlight];
     if (2 * warp < Klen) load_batch(2 * warp, w);
     for (int cw = 2 * warp; cw < Klen; cw += kStride) {
@@ -272,8 +275,8 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
         bf16x8_to_f32(w[r], x);
         float best = -INFINITY;
         for (int g = 0; g < G; ++g) {
-          const float4 qa = reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl];
-          const float4 qb = reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl + 1];
+          const float4 qa = g == 0 ? qa0 : reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl];
+          const float4 qb = g == 0 ? qb0 : reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl + 1];
           float p = qa.x * x[0];
           p = fmaf(qa.y, x[1], p);
           p = fmaf(qa.z, x[2], p);
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
           best = fmaxf(best, p);
         }
         const int c = c0 + r * kHalves;
-        if (hl == 0 && c < Klen) scores[c] = __fdiv_rn(best, a.sqrt_d);
+        if (hl == 0 && c < Klen) scores[c] = best;  // divided by sqrt(D) in the pooling pass
       }
 #pragma unroll
       for (int r = 0; r < kRowsInFlight; ++r) w[r] = wn[r];
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
         }
       }
       p = warp_sum(p);
-      if (lane == 0) lead_scores[c] = __fdiv_rn(p, a.sqrt_d);
+      if (lane == 0) lead_scores[c] = p;  // divided by sqrt(D) in the pooling pass
     }
   }
   if (kHeadSelect) {
@@ -334,11 +337,14 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   }
   if (kHeadSelect || crank == 0) {
 
-  // 3) max_pool1d(kernel=pool_k, stride 1, padding pool_k/2)[:Klen]
+  // 3) scores / sqrt(D) (an IEEE fp32 division, attention.py:376-383 / :324-325) and
+  //    max_pool1d(kernel=pool_k, stride 1, padding pool_k/2)[:Klen]
   //    (attention.py:386-393 / :328-335), as order-preserving bits, computed
   //    once: into the (still unused) selection buffer, then copied over the
   //    raw scores, which nothing reads afterwards; every later pass reads one
-  //    word per key.
+  //    word per key. The division of the window's maximum equals the maximum
+  //    of the divided scores bit for bit (division by a positive constant is
+  //    monotonic in round-to-nearest), so each key is divided once.
   const int pad = pool_k / 2;
   uint32_t* pbits = reinterpret_cast<uint32_t*>(scores);
   {
@@ -350,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
         m = -INFINITY;
         for (int j = lo; j <= hi; ++j) m = fmaxf(m, scores[j]);
       }
-      tmp[c] = order_bits(m);
+      tmp[c] = order_bits(__fdiv_rn(m, a.sqrt_d));
     }
     __syncthreads();
     for (int c = threadIdx.x; c < Klen; c += kThreads) pbits[c] = tmp[c];
