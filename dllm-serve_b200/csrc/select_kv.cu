@@ -145,7 +145,10 @@ DLLM_DEVICE int cand_token(int c, int blk_start, int blk_len) {
   return c < blk_start ? c : c + blk_len;
 }
 
-template <bool kHeadSelect>
+// kGroup (head_select only): more than one query head per KV head. The two
+// cases are separate instantiations so that the grouped scoring's registers
+// do not cost the single-head scoring loop.
+template <bool kHeadSelect, bool kGroup>
 __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int seq = blockIdx.y;
@@ -273,8 +276,8 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
       for (int r = 0; r < kRowsInFlight; ++r) {
         float x[8];
         bf16x8_to_f32(w[r], x);
-        float best = -INFINITY;
-        for (int g = 0; g < G; ++g) {
+        // lane partial of q_avg[g] . k over this lane's 8 dimensions
+        auto dot8 = [&](int g) -> float {
           const float4 qa = g == 0 ? qa0 : reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl];
           const float4 qb = g == 0 ? qb0 : reinterpret_cast<const float4*>(q_avg + g * kD)[2 * hl + 1];
           float p = qa.x * x[0];
@@ -285,9 +288,42 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
           p = fmaf(qb.y, x[5], p);
           p = fmaf(qb.z, x[6], p);
           p = fmaf(qb.w, x[7], p);
+          return p;
+        };
+        float best = -INFINITY;
+        if constexpr (!kGroup) {
+          best = dot8(0);
 #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-          best = fmaxf(best, p);
+          for (int o = 8; o > 0; o >>= 1) best += __shfl_xor_sync(0xffffffffu, best, o);
+        } else if (G <= 8) {
+          // GQA: the 16-lane xor-tree sums of all (up to 8) group heads at once,
+          // as a reduce-scatter: at distance 8, 4, 2 each lane keeps half of its
+          // heads and adds its partner's partials of them, then distance 1; every
+          // head's sum is the same tree (the same bits) as one reduction per
+          // head, in 8 shuffles instead of 4 per head. Lanes 2h, 2h+1 end with
+          // head h; the maximum is then taken over the heads in order (one
+          // shuffle per head).
+          float hs[8];
+#pragma unroll
+          for (int g = 0; g < 8; ++g) hs[g] = g < G ? dot8(g) : 0.f;
+          const bool u8 = (hl & 8) != 0, u4 = (hl & 4) != 0, u2 = (hl & 2) != 0;
+          float h4[4], h2[2];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            h4[i] = (u8 ? hs[4 + i] : hs[i]) + __shfl_xor_sync(0xffffffffu, u8 ? hs[i] : hs[4 + i], 8);
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            h2[i] = (u4 ? h4[2 + i] : h4[i]) + __shfl_xor_sync(0xffffffffu, u4 ? h4[i] : h4[2 + i], 4);
+          float d = (u2 ? h2[1] : h2[0]) + __shfl_xor_sync(0xffffffffu, u2 ? h2[0] : h2[1], 2);
+          d += __shfl_xor_sync(0xffffffffu, d, 1);
+          for (int g = 0; g < G; ++g) best = fmaxf(best, __shfl_sync(0xffffffffu, d, (lane & 16) + 2 * g));
+        } else {
+          for (int g = 0; g < G; ++g) {
+            float p = dot8(g);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+            best = fmaxf(best, p);
+          }
         }
         const int c = c0 + r * kHalves;
         if (hl == 0 && c < Klen) scores[c] = best;  // divided by sqrt(D) in the pooling pass
@@ -567,25 +603,26 @@ cudaError_t launch_select_kv(const SelectArgs& a, bool head_select, int n_seqs, 
   // recorded into a CUDA graph, make no attribute calls).
   // Host threads share these caches; raising the attribute is serialised so
   // that a concurrent smaller request never lowers it under a larger one.
-  static std::atomic<size_t> smem_set[2][64];
+  static std::atomic<size_t> smem_set[3][64];
   static std::mutex raise_mu;
+  const int kind = head_select ? (a.group > 1 ? 2 : 1) : 0;
+  void (*kernel)(SelectArgs) = kind == 0   ? select_kv_kernel<false, false>
+                               : kind == 1 ? select_kv_kernel<true, false>
+                                           : select_kv_kernel<true, true>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  std::atomic<size_t>* have = (dev >= 0 && dev < 64) ? &smem_set[head_select ? 1 : 0][dev] : nullptr;
+  std::atomic<size_t>* have = (dev >= 0 && dev < 64) ? &smem_set[kind][dev] : nullptr;
   if (have == nullptr || have->load(std::memory_order_acquire) < smem) {
     std::lock_guard<std::mutex> lock(raise_mu);
     const size_t target = have != nullptr ? std::max(have->load(), smem) : smem;
-    e = head_select ? cudaFuncSetAttribute(select_kv_kernel<true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)target)
-                    : cudaFuncSetAttribute(select_kv_kernel<false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)target);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)target);
     if (e != cudaSuccess) return e;
     if (have != nullptr) have->store(target, std::memory_order_release);
   }
   if (head_select)
-    return launch_pdl(select_kv_kernel<true>, grid, dim3(kThreads), smem, stream, a);
-  return launch_pdl_cluster(select_kv_kernel<false>, grid, dim3(kThreads), smem, stream, kClusterCtas, a);
+    return launch_pdl(kernel, grid, dim3(kThreads), smem, stream, a);
+  return launch_pdl_cluster(kernel, grid, dim3(kThreads), smem, stream, kClusterCtas, a);
 }
 
 }  // namespace dllm
