@@ -457,8 +457,12 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
   const uint32_t T = prefix;  // order bits are never 0 (NaN-free scores), so T = 0 keeps every key
 
   // 5) compaction: every key above T, and the krem keys equal to T with the
-  //    lowest candidate indices (ties by ascending index), in any order.
-  {
+  //    lowest candidate indices (ties by ascending index), in any order. With
+  //    the whole set sorted every key goes in: a plain copy.
+  if (full_sort) {
+    for (int c = threadIdx.x; c < Klen; c += kThreads)
+      sel[c] = ((uint64_t)pbits[c] << 32) | (uint64_t)(0xffffffffu - (uint32_t)c);
+  } else {
     uint32_t eq_base = 0;
     const uint32_t lt_mask = (1u << lane) - 1u;
     for (int c0 = 0; c0 < Klen; c0 += kThreads) {
