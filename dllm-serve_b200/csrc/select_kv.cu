@@ -543,21 +543,22 @@ __global__ void __launch_bounds__(kThreads, 2) select_kv_kernel(SelectArgs a) {
         const int j = j0 + r * kHalves;
         dst[r] = -1;
         if (j < n_keep) {
+          // the row loads do not wait for the slot (only the store needs it):
+          // both memory latencies overlap
           const int c = (int)(0xffffffffu - (uint32_t)(sel[j] & 0xffffffffu));
-          const int64_t slot = a.slots[slot_off + j];
-          if (slot >= a.num_slots) {
-            if (hl == 0) set_error(a.err, kDevSlotOutOfRange);
-          } else if (slot >= 0) {
-            const int64_t tok = tok_start + cand_token(c, blk_start, blk_len);
-            kv[r][0] = __ldg(reinterpret_cast<const uint4*>(a.k + tok * a.k_tok_stride + (int64_t)h * kD) + hl);
-            kv[r][1] = __ldg(reinterpret_cast<const uint4*>(a.v + tok * a.v_tok_stride + (int64_t)h * kD) + hl);
-            dst[r] = slot;
-          }
+          const int64_t tok = tok_start + cand_token(c, blk_start, blk_len);
+          kv[r][0] = __ldg(reinterpret_cast<const uint4*>(a.k + tok * a.k_tok_stride + (int64_t)h * kD) + hl);
+          kv[r][1] = __ldg(reinterpret_cast<const uint4*>(a.v + tok * a.v_tok_stride + (int64_t)h * kD) + hl);
+          dst[r] = a.slots[slot_off + j];
         }
       }
 #pragma unroll
       for (int r = 0; r < kRowsInFlight; ++r) {
-        if (dst[r] < 0) continue;
+        if (dst[r] < 0) continue;  // negative slot: skipped (padding convention)
+        if (dst[r] >= a.num_slots) {
+          if (hl == 0) set_error(a.err, kDevSlotOutOfRange);
+          continue;
+        }
         reinterpret_cast<uint4*>(a.k_cache + dst[r] * a.cache_tok_stride + (int64_t)h * kD)[hl] = kv[r][0];
         reinterpret_cast<uint4*>(a.v_cache + dst[r] * a.cache_tok_stride + (int64_t)h * kD)[hl] = kv[r][1];
       }

@@ -530,6 +530,47 @@ def test_select_kv_store_bit_exact(dev, case):
     assert torch.equal(kc.cpu().float(), kc_ref) and torch.equal(vc.cpu().float(), vc_ref)
 
 
+@pytest.mark.parametrize("hq,hkv,hs", [(4, 4, True), (8, 2, False)])
+def test_select_kv_store_slot_edges(dev, hq, hkv, hs):
+    """A negative slot skips its selected row and a slot past the cache skips
+    it and sets DLLM_DEV_SLOT_OUT_OF_RANGE; every other selected row lands as
+    with valid slots, and the chosen indices do not change."""
+    from dllmserve_b200 import _native
+
+    D, L, b0, bl, ratio = 128, 200, 50, 32, 0.5
+    g = I.gen(77 + hq)
+    q, k, v = I.grid(g, (L, hq, D)), I.grid(g, (L, hkv, D)), I.grid(g, (L, hkv, D))
+    n = R.num_keep(L - bl, ratio)
+    pages = (n + 255) // 256 + 1
+    num_slots = pages * 256
+    good = torch.randperm(num_slots, generator=g)[:n].to(torch.int32)
+    bad = good.clone()
+    bad[3] = -1
+    bad[7] = num_slots + 5
+    t = lambda x: x.to(dev, torch.bfloat16)
+    desc = torch.tensor([[0, L, b0, bl, n, 0, 0, 3]], dtype=torch.int32, device=dev)
+    out = []
+    for slots in (good, bad):
+        kc = torch.zeros(pages, 256, hkv, D, dtype=torch.bfloat16, device=dev)
+        vc = torch.zeros_like(kc)
+        top = torch.full((n * (hkv if hs else 1),), -1, dtype=torch.int64, device=dev)
+        _status_clear(dev)
+        _ops().select_kv_store(t(q), t(k), t(v), desc, L - bl, hs, kc, vc, slots.to(dev), top)
+        torch.cuda.synchronize()
+        out.append((kc.view(num_slots, -1).cpu(), vc.view(num_slots, -1).cpu(), top.cpu(),
+                    _ops().read_device_status(dev)))
+    (kg, vg, tg, sg), (kb, vb, tb, sb) = out
+    assert sg == 0 and sb == _native.DLLM_DEV_SLOT_OUT_OF_RANGE
+    assert torch.equal(tg, tb)
+    keep = torch.ones(n, dtype=torch.bool)
+    keep[3] = keep[7] = False
+    rows = good[keep].long()
+    assert torch.equal(kb[rows], kg[rows]) and torch.equal(vb[rows], vg[rows])
+    skipped = good[~keep].long()
+    assert not kb[skipped].any() and not vb[skipped].any()
+    assert kg[skipped].any()  # the valid run did write those rows
+
+
 @pytest.mark.parametrize("layout", ["pages", "random", "mixed"])
 @pytest.mark.parametrize("hq,hkv", [(4, 4), (7, 1)])
 def test_attention_paged_cache(dev, layout, hq, hkv):
