@@ -34,7 +34,7 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kD = 128;
 constexpr int kRowsInFlight = 4;                     // candidate rows per half warp per pass
-constexpr int kFullSortMax = 2048;
+constexpr int kFullSortMax = 512;  // up to this many (padded) candidates the whole set is sorted, no select
 // Shared ranking (head_select off) runs as a cluster of kClusterCtas CTAs per
 // sequence: all score a slice of the candidates into the leader's shared
 // memory, the leader selects, all gather a slice of the selected rows.
