@@ -612,7 +612,26 @@ def run_ours(args, lens):
 
         w = (torch.randn(HIDDEN, Hq * HEAD_DIM, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
         steps_tp = max(1, min(args.steps, 20))
-        fused = OprojAllReduce(N, HIDDEN, device=dev)
+        # The fused path must not take the whole line down: the ranks agree on
+        # whether every rank could set it up, and a device error it raises is
+        # recorded and cleared (the other paths' numbers stand).
+        fused, fused_problem = None, None
+        try:
+            fused = OprojAllReduce(N, HIDDEN, device=dev)
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            fused_problem = f"setup failed: {e}"
+        fused_ok = max_over_ranks(0.0 if fused is not None else 1.0) == 0.0
+        if not fused_ok and fused_problem is None:
+            fused_problem = "setup failed on another rank"
+
+        def fused_status_clean(where):
+            nonlocal fused_ok, fused_problem
+            st = max_over_ranks(float(ops.read_device_status(dev, reset=False)))
+            if st != 0.0:
+                fused_ok = False
+                fused_problem = f"device status {int(st)} after {where}"
+                ops.read_device_status(dev, reset=True)
+            return fused_ok
 
         def tp_gemm_only():  # no collective: what the all-reduce adds is measured against this
             for l in range(LAYERS):
@@ -645,25 +664,39 @@ def run_ours(args, lens):
 
         ms_gemm = time_tp(tp_gemm_only)
         ms_nccl = time_tp(tp_nccl)
-        ms_fused = time_tp(tp_fused)
-        # the fused path's result against GEMM + NCCL on the last layer's inputs
+        if ops.read_device_status(dev, reset=False) != 0:
+            raise RuntimeError("a kernel reported a device error before the fused o_proj path")
+        ms_fused, fused_err = None, None
         o = ops.varlen_attention(qs[0], ks[0], vs[0], cu, cu, max_q, scale, out=outs[0])
-        y_ref = row_parallel_oproj(o.view(N, Hq * HEAD_DIM), w, rank=rank)
-        y_f = fused(o.view(N, Hq * HEAD_DIM), w)
-        torch.cuda.synchronize()
-        fused_err = max_over_ranks(float((y_f.float() - y_ref.float()).abs().max()))
-        fused.close()
-        del fused
-        best = min(ms_nccl, ms_fused)
+        if fused_ok:
+            # one call first: a peer that never writes ends within the kernel's wait limit
+            fused(o.view(N, Hq * HEAD_DIM), w)
+            torch.cuda.synchronize()
+        if fused_status_clean("a first call"):
+            ms_fused = time_tp(tp_fused)
+        if fused_ok and fused_status_clean("the timed calls"):
+            # the fused path's result against GEMM + NCCL on the first layer's inputs
+            y_ref = row_parallel_oproj(o.view(N, Hq * HEAD_DIM), w, rank=rank)
+            y_f = fused(o.view(N, Hq * HEAD_DIM), w)
+            torch.cuda.synchronize()
+            fused_err = max_over_ranks(float((y_f.float() - y_ref.float()).abs().max()))
+        if not fused_ok:
+            ms_fused = None
+        if fused is not None:
+            fused.close()
+            del fused
+        best = ms_nccl if ms_fused is None else min(ms_nccl, ms_fused)
         tp_block = {"ms_per_step": best, "step_tokens_per_s": N / (best * 1e-3),
                     "ms_per_step_by_path": {"attention_gemm_no_collective": ms_gemm,
                                             "attention_gemm_nccl_allreduce": ms_nccl,
                                             "attention_fused_oproj_allreduce": ms_fused},
                     "us_per_layer_by_path": {"attention_gemm_no_collective": ms_gemm * 1e3 / LAYERS,
                                              "attention_gemm_nccl_allreduce": ms_nccl * 1e3 / LAYERS,
-                                             "attention_fused_oproj_allreduce": ms_fused * 1e3 / LAYERS},
+                                             "attention_fused_oproj_allreduce":
+                                                 None if ms_fused is None else ms_fused * 1e3 / LAYERS},
                     "allreduce_share_nccl_path": (ms_nccl - ms_gemm) / ms_nccl,
                     "fused_vs_nccl_max_abs_diff": fused_err,
+                    "fused_problem": fused_problem,
                     "includes": "per layer: attention on the rank's heads + o_proj [tokens, Hq*128] x "
                                 "[4096, Hq*128]^T bf16 + all-reduce of [tokens, 4096] bf16; the nccl path "
                                 "is cuBLAS + NCCL, the fused path one dllm_oproj_allreduce launch",
