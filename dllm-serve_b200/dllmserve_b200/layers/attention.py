@@ -8,12 +8,15 @@ and ``forward(q, k, v) -> [N, num_heads * head_dim]`` reading the per-step
 reference's argument order and assertions (attention.py:33-92).
 
 The diffusion path (``context.is_diffusion``, attention.py:150-306) runs as
-  1. one scoring/top-k/store launch per ``head_select`` flavour for the
-     sequences in the "compute cache" state (state 1), and
-  2. one non-causal varlen attention launch over every sequence, whose keys
+  1. one non-causal varlen attention launch over every sequence, whose keys
      are [cached rows read from the paged cache by slot ; fresh rows] for
-     "reuse" sequences (state 2),
-with all per-sequence metadata built once per step (``StepPlan``).
+     "reuse" sequences (state 2), and
+  2. one scoring/top-k/store launch per ``head_select`` flavour for the
+     sequences in the "compute cache" state (state 1),
+with all per-sequence metadata built once per step (``StepPlan``). The
+reference stores the selection before it attends; the two launches touch
+disjoint memory (the selection writes only state-1 sequences' cache slots,
+the attention reads only state-2 ones), so the order changes no result.
 """
 from __future__ import annotations
 
@@ -101,6 +104,18 @@ class Attention(nn.Module):
         H, Hk, D = self.num_heads, self.num_kv_heads, self.head_dim
         if self.record_selection:
             self.last_selection = {}
+        out = torch.empty((q.shape[0], H * D), dtype=q.dtype, device=dev)
+        launch = plan.scratch.get(self._launch_key)
+        if launch is None:
+            # step-level arguments validated once per plan, shared by the layers of this shape
+            launch = ops.prepare_attention(
+                plan.cu, plan.cu, plan.max_rows, plan.total_rows, H, Hk, D, self.scale, dev,
+                slots=plan.slots_c, cu_seqlens_slots=plan.cu_c)
+            plan.scratch[self._launch_key] = launch
+        res = launch(q, k, v, out, self._paged_cache_args() if plan.total_c > 0 else None)
+        # The selection runs after the attention: it writes only the cache slots
+        # of compute-cache sequences, which no launch of this step reads, and
+        # finds this layer's K/V still partly in L2.
         if plan.sel:
             qv, kv_, vv = q.view(-1, H, D), k.view(-1, Hk, D), v.view(-1, Hk, D)
             for head_select in (True, False):
@@ -114,15 +129,7 @@ class Attention(nn.Module):
                     self.last_selection[head_select] = top_idx
                 ops.select_kv_store(qv, kv_, vv, desc, max_klen, head_select,
                                     self.k_cache, self.v_cache, slots, top_idx)
-        out = torch.empty((q.shape[0], H * D), dtype=q.dtype, device=dev)
-        launch = plan.scratch.get(self._launch_key)
-        if launch is None:
-            # step-level arguments validated once per plan, shared by the layers of this shape
-            launch = ops.prepare_attention(
-                plan.cu, plan.cu, plan.max_rows, plan.total_rows, H, Hk, D, self.scale, dev,
-                slots=plan.slots_c, cu_seqlens_slots=plan.cu_c)
-            plan.scratch[self._launch_key] = launch
-        return launch(q, k, v, out, self._paged_cache_args() if plan.total_c > 0 else None)
+        return res
 
     def _paged_cache_args(self):
         """Validated pointer/size arguments of the bound paged cache, recomputed
