@@ -49,7 +49,16 @@ constexpr uint32_t kOffBar = kOffV + kStagesV * kTileBytes;     // barriers
 constexpr uint32_t kNumBars = 2 + 2 * kStagesK + 2 * kStagesV + 2 + 2 + 2 + 1 + 2 * 4;  // + unit ring
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffRing = kOffMisc + 64;                   // kRing unit ids
-constexpr uint32_t kSmemBytes = kOffRing + 16 + 1024;          // + alignment slack
+constexpr int kOrderMaxSeqs = 128;                             // sequences a long-first launch may rank
+constexpr uint32_t kOffOrder = kOffRing + 16;                  // long-first order + its keys
+constexpr uint32_t kSmemBytes = kOffOrder + 8 * kOrderMaxSeqs + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "pair kernel shared memory over the 227 KB opt-in limit");
+// A launch with at most this many units (counted as B * heads * qunits) per SM
+// hands out long sequences first. Config-2 lengths (16 sequences of 419-1,087
+// tokens): 4 heads 40.5 -> 38.8 us, 8 heads 63.4 -> 58.1 us, 16 heads (8.6
+// units per SM) 108.6 -> 106.5 us; at 32 heads (17.3 per SM) long-first is
+// 6 % slower than the sequence order, which then balances as well.
+constexpr int kLongFirstUnitsPerSm = 10;
 
 // barrier indices
 constexpr int BAR_Q = 0;
@@ -262,6 +271,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t q_it = 0;     // units whose Q was loaded (warp 8)
     uint32_t done = 0;     // tiles issued into this ring
     int next_static = (int)blockIdx.x + (int)gridDim.x;  // static order (warp 8, lane 0)
+    int* order = reinterpret_cast<int*>(smem + kOffOrder);
+    if (kq && args.long_first) {
+      // order[r] = the sequence handed out r-th: most key tiles first, ties by
+      // index. key = min(tiles, 2^22) * kOrderMaxSeqs + (kOrderMaxSeqs - 1 - b)
+      // is distinct per sequence (B <= kOrderMaxSeqs) and fits an int; a
+      // sequence's rank is the number of larger keys.
+      int* keys = order + kOrderMaxSeqs;
+      const int B = args.B;
+      for (int b = lane; b < B; b += 32) {
+        const int nk = args.cu_k[b + 1] - args.cu_k[b];
+        const int nc = args.cu_c != nullptr ? args.cu_c[b + 1] - args.cu_c[b] : 0;
+        const int tiles = min((nc + kTileN - 1) / kTileN + (nk + kTileN - 1) / kTileN, 1 << 22);
+        keys[b] = tiles * kOrderMaxSeqs + (kOrderMaxSeqs - 1 - b);
+      }
+      __syncwarp();
+      for (int b = lane; b < B; b += 32) {
+        const int mine = keys[b];
+        int r = 0;
+#pragma unroll 4
+        for (int c = 0; c < B; ++c) r += keys[c] > mine ? 1 : 0;
+        order[r] = b;
+      }
+      __syncwarp();
+    }
+    // position v of the hand-out order -> unit id (identity unless long_first)
+    auto unit_at = [&](int v) -> int {
+      if (!args.long_first) return v;
+      const int per_b = args.n_heads * args.qunits;
+      const int r = v / per_b;
+      return order[r] * per_b + (v - r * per_b);
+    };
     bool ok = true;
     for (uint32_t n = 0; ok; ++n) {
       int u;
@@ -280,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             return r;
           };
           u = n == 0 ? (int)blockIdx.x : claim();
-          while (u < total_units && !decode_unit(u, args).valid) {
+          while (u < total_units && !decode_unit(unit_at(u), args).valid) {
             if (args.head_idx != nullptr) {
               const int hs = (u % (args.n_heads * args.qunits)) / args.qunits;
               const int hq = args.head_idx[hs];
@@ -288,11 +328,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             u = claim();
           }
-          uring[n % kRing] = u < total_units ? u : -2;
+          u = u < total_units ? unit_at(u) : -2;
+          uring[n % kRing] = u;
           mbar_arrive(bar(BAR_UFULL + n % kRing));
         }
         u = __shfl_sync(0xffffffffu, u, 0);
-        if (u >= total_units) break;
+        if (u < 0) break;
       } else {
         u = take_unit(n, true);
         if (u == -1) { ok = false; break; }
@@ -668,6 +709,7 @@ cudaError_t launch_attn_fwd(const CUtensorMap& tmQ, const CUtensorMap& tmK, cons
   if (units == 0) return cudaSuccess;
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   a.total_units = (int)units;
+  a.long_first = a.B <= kOrderMaxSeqs && units <= (long long)kLongFirstUnitsPerSm * num_sms ? 1 : 0;
   const int grid = (int)(units < num_sms ? units : num_sms);
   // Programmatic dependent launch: this grid may start while the previous
   // kernel in the stream finishes; it waits for it in griddep_wait().

@@ -46,6 +46,10 @@ struct AttnKernelArgs {
   int qunits;              // query units per (sequence, head): 256-row tile pairs (pair
                            // kernel) or 128-row tiles (split kernel); set by the launcher
   int total_units;         // B * n_heads * qunits; set by the launcher
+  // Pair kernel: 1 = hand out the units of the sequences with the most key
+  // tiles first (ties by sequence index), 0 = in sequence order. Set by the
+  // launcher; it changes only which CTA computes a unit and when.
+  int long_first;
   // Rotary embedding applied on chip (split kernel only; null positions: off).
   // Query row r and fresh key row r are rotated by cos_sin[positions[r]]
   // between their TMA arrival and the MMA that reads them; cached rows are

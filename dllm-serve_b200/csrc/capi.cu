@@ -235,6 +235,7 @@ int attn_common(const void* q, int64_t q_tok_stride, const void* k, int64_t k_to
   a.qpack = qpack;
   a.qunits = 0;
   a.total_units = 0;
+  a.long_first = 0;
   a.positions = positions;
   a.cos_sin = cos_sin;
   a.max_position = max_position;
