@@ -293,7 +293,8 @@ int kv_copy_common(bool store, const void* key, int64_t key_stride, const void* 
 
 // Scheduler workspace of dllm_attn_varlen_fwd_static_ws: file-scope device
 // memory (one copy per device, zero when the module loads). The attention
-// kernel uses the first DLLM_SCHED_WORKSPACE_INTS words and leaves them zero.
+// kernel uses the first DLLM_SCHED_WORKSPACE_INTS words and leaves them zero;
+// each call also clears them on its stream before the launch.
 constexpr int kStaticWsInts = 64;
 static __device__ __align__(256) int32_t g_static_sched_ws[kStaticWsInts];
 
@@ -375,6 +376,11 @@ int dllm_attn_varlen_fwd_static_ws(const void* q, int64_t q_tok_stride, const vo
                 stream_dev, dev);
   int32_t* ws = static_sched_ws(dev, &e);
   if (ws == nullptr) return cuda_fail(e, "cudaGetSymbolAddress(static scheduler workspace)");
+  // The words are shared by every call on this device and keep what the last
+  // launch left (zero when it ran to its end); clear them on the stream so this
+  // launch starts from zero whatever an earlier call did.
+  e = cudaMemsetAsync(ws, 0, sizeof(int32_t) * DLLM_SCHED_WORKSPACE_INTS, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the static scheduler workspace");
   return attn_common(q, q_tok_stride, k, k_tok_stride, v, v_tok_stride, nullptr, 0, nullptr, 0, o,
                      o_tok_stride, cu_seqlens_q, cu_seqlens_k, nullptr, batch, max_seqlen_q,
                      total_q, total_k, 0, num_heads, num_kv_heads, head_dim, softmax_scale, ws,

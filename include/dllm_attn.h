@@ -153,10 +153,11 @@ DLLM_API int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const voi
  * Set-up: the first call on a device (with that device current) looks up the
  * array's device address with cudaGetSymbolAddress and keeps it for later
  * calls; make that first call before any stream capture. The stream must
- * belong to the current device (DLLM_ERR_INVALID_ARG otherwise). The kernel
- * leaves the words at zero on every exit path, so each call starts from a
- * clean state; calls that overlap in time on one device (several streams or
- * host threads) share the words and race: run them one after another.
+ * belong to the current device (DLLM_ERR_INVALID_ARG otherwise). Each call
+ * clears the words it uses on its stream (cudaMemsetAsync, no allocation)
+ * before the launch, so it starts from zero whatever an earlier call left;
+ * calls that overlap in time on one device (several streams or host threads)
+ * share the words and race: run them one after another.
  * No counterpart in the reference (its flash_attn_varlen_func takes no
  * workspace).
  */

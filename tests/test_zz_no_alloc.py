@@ -7,8 +7,8 @@ the library instead of a caller buffer.
 Checked through the C ABI: two calls in a row write the same output bits as
 dllm_attn_varlen_fwd with a caller workspace (and as the round-robin order)
 and agree with the CPU oracle within the attention tolerance; a launch of
-another shape afterwards is still correct (the kernel leaves the static words
-at zero); the short-query path (max_seqlen_q <= 128) gives the same result as
+another shape afterwards is still correct (each call clears the static words
+on its stream, and the kernel leaves them at zero); the short-query path (max_seqlen_q <= 128) gives the same result as
 the caller-workspace entry. This file sorts last, so a run that stops at the
 first failure has run every other test before it, and it also passes alone
 in a fresh process.
