@@ -152,7 +152,9 @@ DLLM_API int dllm_attn_varlen_fwd(const void* q, int64_t q_tok_stride, const voi
  *
  * Set-up: the first call on a device (with that device current) looks up the
  * array's device address with cudaGetSymbolAddress and keeps it for later
- * calls; make that first call before any stream capture. The stream must
+ * calls; make that first call before any stream capture. The kept address
+ * belongs to the device's current context: after cudaDeviceReset on that
+ * device, do not call this entry point again in the same process. The stream must
  * belong to the current device (DLLM_ERR_INVALID_ARG otherwise). Each call
  * clears the words it uses on its stream (cudaMemsetAsync, no allocation)
  * before the launch, so it starts from zero whatever an earlier call left;
