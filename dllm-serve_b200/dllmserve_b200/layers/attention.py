@@ -46,7 +46,7 @@ def _plan_for(ctx, q: torch.Tensor, num_kv_heads: int):
             setattr(ctx, _PLAN_ATTR, plans)
         except AttributeError:  # a frozen context: rebuild per layer
             pass
-    key = (q.device, q.shape[0], num_kv_heads)
+    key = (q.get_device(), q.shape[0], num_kv_heads)
     plan = plans.get(key)
     if plan is None:
         plan = build_step_plan(ctx, q.device, q.shape[0], num_kv_heads)
@@ -100,23 +100,25 @@ class Attention(nn.Module):
         """q [N, num_heads*D] or [N, num_heads, D]; k, v likewise with
         num_kv_heads; returns [N, num_heads*D]."""
         plan = _plan_for(context, q, self.num_kv_heads)
-        dev = q.device
         H, Hk, D = self.num_heads, self.num_kv_heads, self.head_dim
         if self.record_selection:
             self.last_selection = {}
-        out = torch.empty((q.shape[0], H * D), dtype=q.dtype, device=dev)
+        out = q.new_empty((q.shape[0], H * D))
         launch = plan.scratch.get(self._launch_key)
         if launch is None:
+            dev = q.device
             # step-level arguments validated once per plan, shared by the layers of this shape
             launch = ops.prepare_attention(
                 plan.cu, plan.cu, plan.max_rows, plan.total_rows, H, Hk, D, self.scale, dev,
                 slots=plan.slots_c, cu_seqlens_slots=plan.cu_c)
             plan.scratch[self._launch_key] = launch
-        res = launch(q, k, v, out, self._paged_cache_args() if plan.total_c > 0 else None)
+        # out was made here with the launch's layout (q's dtype and device, [rows, H*D])
+        res = launch(q, k, v, out, self._paged_cache_args() if plan.total_c > 0 else None, out_checked=True)
         # The selection runs after the attention: it writes only the cache slots
         # of compute-cache sequences, which no launch of this step reads, and
         # finds this layer's K/V still partly in L2.
         if plan.sel:
+            dev = q.device
             qv, kv_, vv = q.view(-1, H, D), k.view(-1, Hk, D), v.view(-1, Hk, D)
             for head_select in (True, False):
                 arrs = selection_arrays(plan, head_select, Hk, dev)

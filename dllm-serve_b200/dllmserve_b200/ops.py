@@ -328,23 +328,28 @@ class AttentionLaunch:
         self._status = _status_ptr(dev)
         self._ws: dict = {}
 
-    def __call__(self, q, k, v, out, cache_args=None):
-        """q/out: [rows, Hq*D] or [rows, Hq, D]; k/v likewise with Hkv (any
-        token stride, heads contiguous). Returns out."""
+    def _check(self, name, t, h):
         Hq, Hkv, D = self._heads
-        rows, idx = self._rows, self._dev_index
-        for name, t, h in (("q", q, Hq), ("k", k, Hkv), ("v", v, Hkv), ("out", out, Hq)):
-            if t.dtype is not torch.bfloat16 or t.get_device() != idx or t.shape[0] != rows:
-                ok = False
-            elif t.dim() == 2:
-                ok = t.shape[1] == h * D and t.stride(1) == 1
-            else:
-                ok = (t.dim() == 3 and t.shape[1] == h and t.shape[2] == D and t.stride(2) == 1
-                      and t.stride(1) == D)
-            if not ok:
-                raise ValueError(f"{name}: expected bfloat16 [{rows}, {h}*{D}] or [{rows}, {h}, {D}] with "
-                                 f"contiguous heads on {self._dev}, got {t.dtype} {tuple(t.shape)} "
-                                 f"strides {t.stride()}")
+        sh, st = t.shape, t.stride()
+        if (t.dtype is not torch.bfloat16 or t.get_device() != self._dev_index or sh[0] != self._rows
+                or not ((len(sh) == 2 and sh[1] == h * D and st[1] == 1)
+                        or (len(sh) == 3 and sh[1] == h and sh[2] == D and st[2] == 1 and st[1] == D))):
+            raise ValueError(f"{name}: expected bfloat16 [{self._rows}, {h}*{D}] or [{self._rows}, {h}, {D}] "
+                             f"with contiguous heads on {self._dev}, got {t.dtype} {tuple(sh)} strides {st}")
+
+    def __call__(self, q, k, v, out, cache_args=None, out_checked=False):
+        """q/out: [rows, Hq*D] or [rows, Hq, D]; k/v likewise with Hkv (any
+        token stride, heads contiguous). Returns out. ``out_checked``: the
+        caller made ``out`` itself with this launch's layout (the layer's own
+        output buffer), so its check is skipped."""
+        Hq, Hkv, D = self._heads
+        idx = self._dev_index
+        check = self._check
+        check("q", q, Hq)
+        check("k", k, Hkv)
+        check("v", v, Hkv)
+        if not out_checked:
+            check("out", out, Hq)
         if self._slots is not None:
             if cache_args is None or cache_args[2] != Hkv * D:
                 raise ValueError("a paged launch needs paged_cache_args of num_kv_heads * head_dim rows")
