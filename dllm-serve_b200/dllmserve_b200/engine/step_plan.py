@@ -160,9 +160,10 @@ class _Staging:
         return i, self.bufs[i]
 
     def done(self, i):
-        ev = torch.cuda.Event()
+        ev = self.events[i]
+        if ev is None:  # one event per buffer, re-recorded at each use
+            ev = self.events[i] = torch.cuda.Event()
         ev.record()
-        self.events[i] = ev
 
 
 _STAGING: dict = {}
@@ -210,7 +211,7 @@ def _device_plan(ctx, device, total_rows, num_kv_heads, infos, slot_lists) -> "S
                      int(ss.block_len), ratio_bits, int(pool) | (int(bool(ss.config.head_select)) << 32),
                      sm.data_ptr(), sm.numel(), 0])
     buf[:B] = torch.tensor(rows, dtype=torch.int64)
-    with torch.cuda.device(device):
+    with ops._on_device(device):
         dev_rows = torch.empty((B, _native.PLAN_SEQ_FIELDS), dtype=torch.int64, device=device)
         dev_rows.copy_(buf[:B], non_blocking=True)
         staging.done(si)

@@ -57,13 +57,23 @@ def _require_cuda(*ts: torch.Tensor) -> torch.device:
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_raw_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
+def _current_device() -> int:
+    """torch.cuda.current_device() without its lazy-initialisation checks
+    (about a microsecond per call); only called once the inputs are CUDA
+    tensors, i.e. after CUDA was initialised."""
+    if _raw_device is not None:
+        return _raw_device()
+    return torch.cuda.current_device()
 
 
 def _stream_ptr() -> int:
     """cudaStream_t of the current stream on the current device (the raw query
     is several microseconds cheaper per call than building a Stream object)."""
     if _raw_stream is not None:
-        return _raw_stream(torch.cuda.current_device())
+        return _raw_stream(_current_device())
     return torch.cuda.current_stream().cuda_stream
 
 
@@ -80,7 +90,7 @@ _CURRENT = _Current()
 
 def _on_device(dev: torch.device):
     """torch.cuda.device(dev), or a no-op context when dev is already current."""
-    if dev.index is None or dev.index == torch.cuda.current_device():
+    if dev.index is None or dev.index == _current_device():
         return _CURRENT
     return torch.cuda.device(dev)
 
@@ -328,14 +338,17 @@ class AttentionLaunch:
         self._status = _status_ptr(dev)
         self._ws: dict = {}
 
-    def _check(self, name, t, h):
-        Hq, Hkv, D = self._heads
+    def _check(self, name, t, h) -> int:
+        """Raises unless t is a bf16 [rows, h*D] / [rows, h, D] tensor with
+        contiguous heads on the launch's device; returns its token stride."""
+        D = self._heads[2]
         sh, st = t.shape, t.stride()
         if (t.dtype is not torch.bfloat16 or t.get_device() != self._dev_index or sh[0] != self._rows
                 or not ((len(sh) == 2 and sh[1] == h * D and st[1] == 1)
                         or (len(sh) == 3 and sh[1] == h and sh[2] == D and st[2] == 1 and st[1] == D))):
             raise ValueError(f"{name}: expected bfloat16 [{self._rows}, {h}*{D}] or [{self._rows}, {h}, {D}] "
                              f"with contiguous heads on {self._dev}, got {t.dtype} {tuple(sh)} strides {st}")
+        return st[0]
 
     def __call__(self, q, k, v, out, cache_args=None, out_checked=False):
         """q/out: [rows, Hq*D] or [rows, Hq, D]; k/v likewise with Hkv (any
@@ -345,11 +358,10 @@ class AttentionLaunch:
         Hq, Hkv, D = self._heads
         idx = self._dev_index
         check = self._check
-        check("q", q, Hq)
-        check("k", k, Hkv)
-        check("v", v, Hkv)
-        if not out_checked:
-            check("out", out, Hq)
+        qs0 = check("q", q, Hq)
+        ks0 = check("k", k, Hkv)
+        vs0 = check("v", v, Hkv)
+        os0 = out.stride(0) if out_checked else check("out", out, Hq)
         if self._slots is not None:
             if cache_args is None or cache_args[2] != Hkv * D:
                 raise ValueError("a paged launch needs paged_cache_args of num_kv_heads * head_dim rows")
@@ -363,8 +375,8 @@ class AttentionLaunch:
                 ws = sched_workspace(self._dev, stream)
                 if ws:
                     self._ws[stream] = ws
-            rc = self._fn(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
-                          *mid, out.data_ptr(), out.stride(0), *self._tail, ws, self._status, stream)
+            rc = self._fn(q.data_ptr(), qs0, k.data_ptr(), ks0, v.data_ptr(), vs0,
+                          *mid, out.data_ptr(), os0, *self._tail, ws, self._status, stream)
         if rc:
             _native.check(rc, "varlen_attention")
         LAUNCHES[0] += 1
