@@ -75,8 +75,6 @@ constexpr int kRing = 4;                         // unit ids published ahead of 
 constexpr int BAR_UFULL = BAR_DRAIN + 1;         // kRing: unit id published
 constexpr int BAR_UEMPTY = BAR_UFULL + kRing;    // kRing: every role read it
 
-DLLM_DEVICE int row_in_tile_of(int tid) { return tid & 127; }
-
 struct KvTile {
   int seg;    // 0 = cached, 1 = fresh
   int row0;   // first row in the segment's source tensor

@@ -88,8 +88,6 @@ constexpr uint32_t kOffXch = kOffMisc + 64;                     // float2 per qu
 constexpr uint32_t kSmemBytes = kOffXch + kTileM * 8 + 1024;    // + alignment slack
 static_assert(kSmemBytes <= 232448, "over the sm_100a per-CTA shared-memory limit");
 
-DLLM_DEVICE int row_in_tile_of(int tid) { return tid & 127; }
-
 struct KvTile {
   int seg;    // 0 = cached, 1 = fresh
   int row0;   // first row in the segment's source tensor

@@ -79,7 +79,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc + 16);
-  volatile int* bcast = reinterpret_cast<volatile int*>(smem + kOffMisc + 32);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
